@@ -1,0 +1,339 @@
+#!/usr/bin/env python
+"""Benchmark of the fused Q4_K GEMV (and the CPU reference beside it).
+
+Workload (the headline metric): one Q4_K GEMV of 14336 output rows over 4096
+inputs (the Llama-3-8B FFN gate/up shape), fp32 x ~ N(0, 1), seeded synthetic
+GGUF weights.  A step is one GEMV.  The weights rotate over enough resident
+copies that the set is larger than three times the L2, so every step streams
+its 33 MB from HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  `value` is whole-job HBM GB/s of algorithmic
+bytes (weights + x + y) with inputs resident; `e2e` is the same metric through
+the GpuOffload-shaped C ABI call with host x and y (copies in the timed
+region).  Under torchrun every rank runs its own GEMV stream (weak scaling, no
+data-path collective); the time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+IN_DIM, OUT_DIM, DTYPE = 4096, 14336, 12
+WORKLOAD = "q4k_gemv_14336x4096"
+METRIC = "Q4_K GEMV HBM GB/s (% of peak) @4096x14336"
+
+
+def algorithmic_bytes(in_dim: int, out_dim: int, dtype: int, batch: int = 1) -> int:
+    """Weight bytes + 4*B*in + 4*B*out (each weight byte, x and y touched once)."""
+    be, bb = {12: (256, 144), 14: (256, 210), 8: (32, 34), 2: (32, 18)}[dtype]
+    return in_dim * out_dim // be * bb + 4 * batch * in_dim + 4 * batch * out_dim
+
+
+def measured_peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def committed_traffic(kernel: str, workload: str):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get(f"{kernel}@{workload}")
+    except (OSError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def cpu_gemv_rate(threads: int, target_s: float, max_calls: int | None = None) -> dict:
+    """The oracle's port of the reference AVX2 matvec_q4k on this host's cores (CPU baseline)."""
+    from oracle import oracle as O
+    from m3_avm_b200 import synth
+
+    raw = synth.weights(DTYPE, IN_DIM, OUT_DIM, seed=1)
+    x = synth.activations(IN_DIM, seed=2)
+    O.matvec_quant(x, raw, DTYPE, IN_DIM, OUT_DIM, threads=threads)  # warm
+    times = []
+    t_end = time.perf_counter() + target_s
+    while time.perf_counter() < t_end and (max_calls is None or len(times) < max_calls):
+        t0 = time.perf_counter()
+        O.matvec_quant(x, raw, DTYPE, IN_DIM, OUT_DIM, threads=threads)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    gbs = algorithmic_bytes(IN_DIM, OUT_DIM, DTYPE) / med / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} full {OUT_DIM}x{IN_DIM} Q4_K GEMVs (C restatement of the reference AVX2 "
+                      f"matvec_q4k, {threads} OpenMP threads), median {med * 1e3:.3f} ms",
+            "median_s": med}
+
+
+def run_reference(args) -> int:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    from m3_avm_b200 import synth
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    raw = synth.weights(DTYPE, IN_DIM, OUT_DIM, seed=1)
+    x = synth.activations(IN_DIM, seed=2)
+    # one step = one full GEMV on the host cores, unless K of them would not fit
+    # in ~2 minutes; then a step is a contiguous slice of rows of that GEMV.
+    t0 = time.perf_counter()
+    O.matvec_quant(x, raw, DTYPE, IN_DIM, OUT_DIM, threads=threads)
+    one = time.perf_counter() - t0
+    rows = OUT_DIM
+    budget = 120.0
+    if one * (args.steps + args.warmup) > budget:
+        rows = max(8, int(OUT_DIM * budget / (one * (args.steps + args.warmup))))
+    row_bytes = IN_DIM // 256 * 144
+    sub = raw[: rows * row_bytes]
+    for _ in range(args.warmup):
+        O.matvec_quant(x, sub, DTYPE, IN_DIM, rows, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.matvec_quant(x, sub, DTYPE, IN_DIM, rows, threads=threads)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    gbs = algorithmic_bytes(IN_DIM, rows, DTYPE) / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "rows_per_step": rows, "in_dim": IN_DIM, "dtype": "Q4_K"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{rows} of {OUT_DIM} rows x {IN_DIM} Q4_K per step (C restatement of the "
+                                   f"reference AVX2 matvec_q4k; the Rust crate cannot be built here)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args) -> int:
+    import torch
+    import torch.distributed as dist
+
+    from m3_avm_b200 import _lib, synth
+    from m3_avm_b200.inference_gpu import GpuOffload
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    lib = _lib.load()
+    dev = torch.device("cuda", local)
+    props = torch.cuda.get_device_properties(dev)
+    l2 = getattr(props, "L2_cache_size", 126 * 1024 * 1024) or 126 * 1024 * 1024
+
+    raw = synth.weights(DTYPE, IN_DIM, OUT_DIM, seed=1 + rank)
+    wbytes = raw.size
+    n_copies = max(2, math.ceil(3 * l2 / wbytes))
+    g = GpuOffload.try_new(IN_DIM, OUT_DIM, device=local)
+    if g is None:
+        raise RuntimeError("GpuOffload.try_new failed: " + _lib.last_error())
+    for c in range(n_copies):
+        if not g.upload(c, DTYPE, raw, IN_DIM, OUT_DIM):
+            raise RuntimeError("upload failed: " + _lib.last_error())
+    x = torch.from_numpy(synth.activations(IN_DIM, seed=2)).to(dev)
+    y = torch.empty(OUT_DIM, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        g.matvec_dev(i % n_copies, x, y, stream=stream.cuda_stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.25)
+    barrier()
+    launches0 = int(lib.m3g_launch_count())
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    launches = int(lib.m3g_launch_count()) - launches0
+    ms = ev0.elapsed_time(ev1)
+    barrier()
+    clocks = sampler.stop()
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    per_step_s = ms_max / 1e3 / args.steps
+    abytes = algorithmic_bytes(IN_DIM, OUT_DIM, DTYPE)
+    value = abytes * world / per_step_s / 1e9
+
+    # e2e: host x -> device, GEMV, device y -> host, through the C ABI offload call.
+    xh = synth.activations(IN_DIM, seed=2)
+    e2e_steps = min(args.steps, 5000)
+    for i in range(min(args.warmup, 50)):
+        g.matvec(i % n_copies, xh, IN_DIM, OUT_DIM)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        if g.matvec(i % n_copies, xh, IN_DIM, OUT_DIM) is None:
+            raise RuntimeError("offload matvec failed: " + _lib.last_error())
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_val = abytes * world / float(te.item()) / 1e9
+
+    status = ctypes_status(lib, local)
+    peaks, kind = measured_peaks()
+    peak = float(peaks["hbm_gbs"])
+    achieved = abytes / per_step_s / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": kind,
+                "traffic": committed_traffic("k_gemv_stream", WORKLOAD), "kernel": "k_gemv_stream<FmtQ4K>",
+                "algorithmic_bytes_per_launch": abytes}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+        cpu = cpu_gemv_rate(threads, target_s=args.cpu_seconds)
+        cpu.pop("median_s", None)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 6), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "dtype": "Q4_K", "in_dim": IN_DIM, "out_dim": OUT_DIM,
+                       "weight_copies": n_copies, "weight_set_mb": round(n_copies * wbytes / 2**20, 1),
+                       "l2_mb": round(l2 / 2**20, 1), "l2": "inputs larger than L2 (rotating weight copies)",
+                       "parallelism": f"replicas{world}"},
+            "pct_of_measured_hbm_peak": round(100 * achieved / peak, 2),
+            "pct_of_8tbps_spec": round(100 * achieved / 8000.0, 2),
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": 4 * IN_DIM,
+                    "d2h_bytes_per_step": 4 * OUT_DIM, "us_per_call": round(float(te.item()) * 1e6, 2),
+                    "api": "m3g_offload_matvec (host x/y, resident weights)"},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    g.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def ctypes_status(lib, device):
+    import ctypes
+
+    out = ctypes.c_uint32()
+    lib.m3g_device_status(device, ctypes.byref(out), 0)
+    return int(out.value)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,174 @@
+/*
+ * m3gemv.h -- C ABI of the B200 (sm_100a) fused dequantise-and-matvec library.
+ *
+ * This is the drop-in boundary for the fused quantised GEMV path of m3_avm:
+ * the GGUF block decoders of src/quant.rs and the fused kernels of
+ * src/matvec_quant.rs, plus the per-tensor offload shape of
+ * src/inference_gpu.rs.  Paths in the citations are relative to the m3_avm
+ * source tree.
+ *
+ * Conventions shared by every entry point:
+ *   - dtype uses ggml numbering: 0 F32, 1 F16, 2 Q4_0, 8 Q8_0, 12 Q4_K,
+ *     13 (Q5_K slot, decoded as Q4_K exactly as the reference does), 14 Q6_K.
+ *   - Weights are GGUF bytes, K = in_dim fastest: y[j] = sum_i x[i] * W[i + j*in_dim].
+ *     A block may straddle two output rows when in_dim is not a multiple of
+ *     the block size; every entry point accepts that layout.
+ *   - Return value: M3G_OK (0) on success, a negative M3G_E* code otherwise.
+ *     M3G_ENONE is the reference's `None` / `false`: an unsupported dtype or a
+ *     shape/length that the reference also rejects.  m3g_last_error() gives
+ *     a message for the calling thread.
+ *   - "_dev" entry points take device pointers and a cudaStream_t passed as
+ *     void* (NULL = the legacy default stream); they enqueue work and return
+ *     without synchronising.  The other entry points take host pointers and
+ *     return when the result is in host memory.
+ *   - Nothing here panics or aborts: failures never propagate beyond the
+ *     return code (the policy of src/inference_gpu.rs:9-10).
+ */
+#ifndef M3GEMV_H
+#define M3GEMV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(M3G_BUILD_LIB) && defined(__GNUC__)
+#define M3G_API __attribute__((visibility("default")))
+#else
+#define M3G_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define M3G_OK 0
+#define M3G_ENONE (-1)      /* reference returns None / false                 */
+#define M3G_EINVAL (-2)     /* bad argument (null pointer, misaligned, ...)   */
+#define M3G_ECUDA (-3)      /* CUDA runtime error                             */
+#define M3G_ENOMEM (-4)     /* device or pinned allocation failed             */
+#define M3G_ENCCL (-5)      /* NCCL error                                     */
+#define M3G_ETIMEOUT (-6)   /* a bounded device-side wait gave up             */
+#define M3G_ENOTFOUND (-7)  /* tensor index not uploaded                      */
+#define M3G_EPANIC (-8)     /* the reference would panic (assert! on sizes)   */
+
+#define M3G_DTYPE_F32 0u
+#define M3G_DTYPE_F16 1u
+#define M3G_DTYPE_Q4_0 2u
+#define M3G_DTYPE_Q8_0 8u
+#define M3G_DTYPE_Q4_K 12u
+#define M3G_DTYPE_Q5_K_AS_Q4_K 13u
+#define M3G_DTYPE_Q6_K 14u
+
+/* Library ABI version (bumped on any signature change). */
+M3G_API int m3g_abi_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+M3G_API const char* m3g_last_error(void);
+
+/* ---------------------------------------------------------------- host-side rules */
+
+/* Bytes needed for n elements of a fused-kernel dtype.
+ * Replaces quant_raw_len (src/matvec_quant.rs:51-83): M3G_ENONE where it
+ * returns None (dtype without a fused kernel, n not a multiple of the block). */
+M3G_API int m3g_quant_raw_len(uint32_t dtype, uint64_t n, uint64_t* out_len);
+
+/* f32 -> bf16 bits, round-to-nearest-even with a quiet-NaN guard.
+ * Replaces f32_to_bf16_bits (src/quant.rs:186-194). */
+M3G_API uint16_t m3g_f32_to_bf16_bits(float x);
+
+/* bf16 bits -> f32, exact.  Replaces bf16_bits_to_f32 (src/quant.rs:197-199). */
+M3G_API float m3g_bf16_bits_to_f32(uint16_t b);
+
+/* One Q4_0 / Q8_0 block from 32 floats (src_len must be 32).  M3G_ENONE where
+ * the reference returns false (wrong length, non-finite input, short dst).
+ * Replace quantize_q4_0 (src/quant.rs:206-234), quantize_q8_0 (:239-264). */
+M3G_API int m3g_quantize_q4_0(const float* src, uint64_t src_len, uint8_t* dst, uint64_t dst_len);
+M3G_API int m3g_quantize_q8_0(const float* src, uint64_t src_len, uint8_t* dst, uint64_t dst_len);
+
+/* ---------------------------------------------------------------- decoders (GPU) */
+
+/* Decode n elements of `dtype` to f32, bit-exact with the reference decoders.
+ * Replaces dequantize (src/quant.rs:120-173) and, with a fixed dtype,
+ * dequant_q4_0 (:9), dequant_q4_k (:41), dequant_q6_k (:76).
+ * M3G_ENONE where dequantize returns false; M3G_EPANIC where the reference's
+ * dequant_q4_0/dequant_q4_k would hit assert! (source shorter than n needs). */
+M3G_API int m3g_dequantize(const uint8_t* src, uint64_t src_len, uint32_t dtype, float* dst, uint64_t n);
+M3G_API int m3g_dequantize_dev(const uint8_t* src, uint64_t src_len, uint32_t dtype, float* dst, uint64_t n,
+                       void* stream);
+
+/* ---------------------------------------------------------------- fused GEMV (GPU) */
+
+/* y[out_dim] = W x for GGUF weight bytes `raw`, host buffers.
+ * Replaces matvec_quant (src/matvec_quant.rs:87-109) including its None rules
+ * (x_len != in_dim, zero dims, dtype without a fused kernel, raw too short),
+ * and with a fixed dtype matvec_q4k (:221), matvec_q6k (:361),
+ * matvec_q4_0 (:368), matvec_q8_0 (:375).  The weights are copied to the
+ * device on every call; use the offload context below to keep them resident. */
+M3G_API int m3g_matvec_quant(const float* x, uint64_t x_len, const uint8_t* raw, uint64_t raw_len, uint32_t dtype,
+                     uint64_t in_dim, uint64_t out_dim, float* y);
+
+/* Device-pointer form: Y[batch][out_dim] = X[batch][in_dim] W^T with
+ * row-major X and Y.  `raw` must be 16-byte aligned. */
+M3G_API int m3g_matvec_quant_dev(const float* x, const uint8_t* raw, uint64_t raw_len, uint32_t dtype,
+                         uint64_t in_dim, uint64_t out_dim, uint64_t batch, float* y, void* stream);
+
+/* ---------------------------------------------------------------- resident offload */
+
+/* Per-tensor resident weights, the GpuOffload shape of src/inference_gpu.rs:40-238:
+ * weights are uploaded once in their native block layout; each matvec moves only
+ * x and y.  A context belongs to one device and owns one stream; calls on one
+ * context must not overlap (the reference calls it from one thread). */
+typedef struct m3g_offload m3g_offload;
+
+/* GpuOffload::try_new (src/inference_gpu.rs:58): M3G_ECUDA when no device. */
+M3G_API int m3g_offload_create(int device, uint64_t max_in, uint64_t max_out, m3g_offload** out);
+
+/* GpuOffload::upload (src/inference_gpu.rs:131-177): M3G_ENONE for a dtype
+ * without a fused kernel, zero dims, or raw_len != quant_raw_len(dtype, in*out).
+ * Re-uploading a tidx replaces it. */
+M3G_API int m3g_offload_upload(m3g_offload* ctx, uint64_t tidx, uint32_t dtype, const uint8_t* raw, uint64_t raw_len,
+                       uint64_t in_dim, uint64_t out_dim);
+
+/* GpuOffload::matvec (src/inference_gpu.rs:188-237), host x and y:
+ * M3G_ENOTFOUND if tidx is not resident, M3G_ENONE if dims differ from the
+ * upload or exceed max_in/max_out. */
+M3G_API int m3g_offload_matvec(m3g_offload* ctx, uint64_t tidx, const float* x, uint64_t in_dim, uint64_t out_dim,
+                       float* y);
+
+/* Batched form of the above: X[batch][in_dim] -> Y[batch][out_dim], host buffers. */
+M3G_API int m3g_offload_matvec_batch(m3g_offload* ctx, uint64_t tidx, const float* x, uint64_t batch, uint64_t in_dim,
+                             uint64_t out_dim, float* y);
+
+/* Device-resident form for callers that keep activations on the GPU:
+ * x and y are device pointers, enqueued on `stream` (NULL = the context's own). */
+M3G_API int m3g_offload_matvec_dev(m3g_offload* ctx, uint64_t tidx, const float* x, uint64_t batch, float* y,
+                           void* stream);
+
+/* GpuOffload::offloaded (:179) -> 1/0, tensor_count (:183), the `calls`
+ * counter (:50) and the device pointer of a resident tensor's bytes. */
+M3G_API int m3g_offload_offloaded(const m3g_offload* ctx, uint64_t tidx);
+M3G_API uint64_t m3g_offload_tensor_count(const m3g_offload* ctx);
+M3G_API uint64_t m3g_offload_calls(const m3g_offload* ctx);
+M3G_API const uint8_t* m3g_offload_tensor_ptr(const m3g_offload* ctx, uint64_t tidx);
+
+M3G_API void m3g_offload_destroy(m3g_offload* ctx);
+
+/* ---------------------------------------------------------------- diagnostics */
+
+/* Error word the kernels of `device` set when a bounded wait gives up
+ * (bit 0: a staged-copy wait timed out).  clear != 0 resets it.  Synchronises
+ * the device. */
+M3G_API int m3g_device_status(int device, uint32_t* out, int clear);
+
+/* Number of kernel launches this library has enqueued in this process. */
+M3G_API uint64_t m3g_launch_count(void);
+
+/* Launch-shape knobs of the streaming GEMV ("stage_bytes", "ctas_per_sm",
+ * "max_stages") and "force_generic" (route every GEMV through the
+ * row-straddling generic kernel).  Process-wide; M3G_ENONE for an unknown key
+ * or out-of-range value.  No counterpart in the reference. */
+M3G_API int m3g_set_tuning(const char* key, int64_t value);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* M3GEMV_H */

@@ -1,0 +1,718 @@
+// m3g_api.cu -- C ABI of libm3gemv: argument rules, launch planning and the
+// resident-offload context.  The rules follow the reference's Rust API for the
+// path (src/matvec_quant.rs:51-109, src/quant.rs:120-173,
+// src/inference_gpu.rs:58-237); the compute is the sm_100a kernels of
+// m3g_kernels.cu.  There is no CPU fallback: without a device every compute
+// entry point returns M3G_ECUDA.
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/m3gemv.h"
+#include "m3g_internal.h"
+
+namespace {
+
+thread_local std::string t_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorMemoryAllocation ? M3G_ENOMEM : M3G_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define M3G_CUDA(call)                                   \
+  do {                                                   \
+    cudaError_t e_ = (call);                             \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+  } while (0)
+
+// ---------------------------------------------------------------- formats
+struct FmtInfo {
+  int fmt;         // kernel format id (13 maps to 12)
+  int be;          // elements per block
+  int bb;          // bytes per block
+  int unit_elems;  // elements per thread unit in the streaming kernel
+};
+
+bool fmt_info(uint32_t dtype, FmtInfo& f) {
+  switch (dtype) {
+    case 12: case 13: f = {12, 256, 144, 64}; return true;
+    case 14: f = {14, 256, 210, 64}; return true;
+    case 8: f = {8, 32, 34, 32}; return true;
+    case 2: f = {2, 32, 18, 32}; return true;
+    default: return false;
+  }
+}
+
+// quant_raw_len (src/matvec_quant.rs:51-83).
+bool raw_len_rule(uint32_t dtype, uint64_t n, uint64_t& out) {
+  FmtInfo f;
+  if (!fmt_info(dtype, f)) return false;
+  if (n % static_cast<uint64_t>(f.be)) return false;
+  out = (n / f.be) * f.bb;
+  return true;
+}
+
+// ---------------------------------------------------------------- tuning
+struct Tuning {
+  int64_t stage_bytes = 16384;  // target bytes per pipeline stage
+  int64_t ctas_per_sm = 2;
+  int64_t max_stages = 8;
+  int64_t force_generic = 0;    // route every GEMV through the generic kernel (parity tests)
+};
+Tuning g_tune;
+
+// ---------------------------------------------------------------- per-device state
+struct DevState {
+  bool ready = false;
+  int sms = 0;
+  int smem_per_sm = 0;
+  int smem_optin = 0;
+  uint32_t* status = nullptr;
+};
+std::mutex g_dev_mu;
+std::vector<DevState> g_dev;
+
+int dev_state(int device, DevState** out) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n <= 0) return fail(M3G_ECUDA, "no CUDA device: %s", cudaGetErrorString(e));
+  if (device < 0 || device >= n) return fail(M3G_EINVAL, "device %d out of range [0,%d)", device, n);
+  if (static_cast<int>(g_dev.size()) < n) g_dev.resize(n);
+  DevState& d = g_dev[device];
+  if (!d.ready) {
+    int prev = 0;
+    M3G_CUDA(cudaGetDevice(&prev));
+    M3G_CUDA(cudaSetDevice(device));
+    M3G_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device));
+    M3G_CUDA(cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device));
+    M3G_CUDA(cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    void* p = nullptr;
+    M3G_CUDA(cudaMalloc(&p, 256));
+    M3G_CUDA(cudaMemset(p, 0, 256));
+    d.status = static_cast<uint32_t*>(p);
+    d.ready = true;
+    M3G_CUDA(cudaSetDevice(prev));
+  }
+  *out = &d;
+  return M3G_OK;
+}
+
+int current_dev_state(DevState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(M3G_ECUDA, "no CUDA device: %s", cudaGetErrorString(e));
+  return dev_state(dev, out);
+}
+
+// ---------------------------------------------------------------- GEMV planning
+struct StreamPlan {
+  m3g::StreamArgs a;
+  int threads = 0, grid = 0, upt = 0;
+  size_t smem = 0;
+};
+
+bool plan_stream(const FmtInfo& f, long long in_dim, long long rows, const uint8_t* w, const DevState& ds,
+                 StreamPlan& p) {
+  if (g_tune.force_generic) return false;
+  if (in_dim % f.be) return false;  // blocks straddle rows
+  const long long RB = (in_dim / f.be) * f.bb;
+  if (RB % 16 || reinterpret_cast<uintptr_t>(w) % 16) return false;
+  if (RB > (1 << 20) || rows > (1ll << 31) - 1) return false;
+  const long long U = in_dim / f.unit_elems;
+  int upt = 0, TS = 0;
+  for (int cand = 1; cand <= 2; ++cand) {
+    long long t = (U + cand - 1) / cand;
+    t = (t + 31) / 32 * 32;
+    if (t <= 256) { upt = cand; TS = static_cast<int>(t); break; }
+  }
+  if (!upt) return false;
+  const int RPI = std::max(1, 256 / TS);
+  const int threads = TS * RPI;
+  const int WPS = TS / 32;
+  const long long ctas_per_sm = std::max<int64_t>(1, g_tune.ctas_per_sm);
+  const long long budget =
+      std::min<long long>(ds.smem_optin, ds.smem_per_sm / ctas_per_sm - 1024);
+  long long m = std::max<long long>(1, std::min<long long>(TS, g_tune.stage_bytes / (RPI * RB)));
+  for (;; --m) {
+    const long long R = RPI * m;
+    const long long stride = (R * RB + 16 + 127) / 128 * 128;
+    const long long red = 2 * R * WPS * 4;
+    long long NS = std::min<long long>(g_tune.max_stages, (budget - red - 8 * g_tune.max_stages) / stride);
+    if (NS >= 2) {
+      p.a.R = static_cast<int>(R);
+      p.a.NS = static_cast<int>(NS);
+      p.a.stage_stride = static_cast<int>(stride);
+      p.smem = static_cast<size_t>(NS * stride + 8 * NS + red);
+      break;
+    }
+    if (m == 1) return false;
+  }
+  const long long grid_target = static_cast<long long>(ds.sms) * ctas_per_sm;
+  const long long rpc = std::max<long long>(1, (rows + grid_target - 1) / grid_target);
+  p.a.rows = static_cast<int>(rows);
+  p.a.RB = static_cast<int>(RB);
+  p.a.U = static_cast<int>(U);
+  p.a.TS = TS;
+  p.a.RPI = RPI;
+  p.a.rows_per_cta = static_cast<int>(rpc);
+  p.threads = threads;
+  p.grid = static_cast<int>((rows + rpc - 1) / rpc);
+  p.upt = upt;
+  return true;
+}
+
+// y[out_dim] = W x on `st`; w/x/y device pointers.
+int gemv_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const float* x, float* y,
+                long long in_dim, long long out_dim, cudaStream_t st) {
+  StreamPlan p;
+  if (plan_stream(f, in_dim, out_dim, w, ds, p)) {
+    p.a.w = w;
+    p.a.x = x;
+    p.a.y = y;
+    p.a.status = ds.status;
+    cudaError_t e = m3g::launch_gemv_stream(f.fmt, p.a, p.threads, p.grid, p.smem, p.upt, st);
+    if (e != cudaSuccess) return cuda_fail(e, "k_gemv_stream launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return M3G_OK;
+  }
+  const long long nblocks = in_dim * out_dim / f.be;
+  M3G_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * static_cast<size_t>(out_dim), st));
+  const long long want = (nblocks + 7) / 8;
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, 8ll * ds.sms)));
+  cudaError_t e = m3g::launch_gemv_generic(f.fmt, w, x, y, in_dim, nblocks, grid, st);
+  if (e != cudaSuccess) return cuda_fail(e, "k_gemv_generic launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return M3G_OK;
+}
+
+int gemv_batch_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const float* x, float* y,
+                      long long in_dim, long long out_dim, long long batch, cudaStream_t st) {
+  for (long long b = 0; b < batch; ++b) {
+    int rc = gemv_launch(ds, f, w, x + b * in_dim, y + b * out_dim, in_dim, out_dim, st);
+    if (rc) return rc;
+  }
+  return M3G_OK;
+}
+
+int check_status(const DevState& ds) {
+  uint32_t s = 0;
+  M3G_CUDA(cudaMemcpy(&s, ds.status, sizeof s, cudaMemcpyDeviceToHost));
+  if (s & m3g::kStatusCopyTimeout) {
+    cudaMemset(ds.status, 0, sizeof s);
+    return fail(M3G_ETIMEOUT, "a staged weight copy did not complete in time");
+  }
+  return M3G_OK;
+}
+
+// Shape rules shared by the GEMV entry points (src/matvec_quant.rs:94-101).
+int gemv_rules(uint32_t dtype, uint64_t raw_len, uint64_t in_dim, uint64_t out_dim, FmtInfo& f) {
+  if (in_dim == 0 || out_dim == 0) return fail(M3G_ENONE, "zero dimension");
+  if (in_dim > (1ull << 40) / out_dim) return fail(M3G_ENONE, "in_dim*out_dim overflows");
+  uint64_t need = 0;
+  if (!raw_len_rule(dtype, in_dim * out_dim, need))
+    return fail(M3G_ENONE, "dtype %u has no fused kernel for %llu elements", dtype,
+                static_cast<unsigned long long>(in_dim * out_dim));
+  if (raw_len < need)
+    return fail(M3G_ENONE, "raw has %llu bytes, needs %llu", static_cast<unsigned long long>(raw_len),
+                static_cast<unsigned long long>(need));
+  if (in_dim > (1ull << 31) || out_dim > (1ull << 31)) return fail(M3G_EINVAL, "dimension too large");
+  fmt_info(dtype, f);
+  return M3G_OK;
+}
+
+// RAII device buffer for the host-pointer entry points.
+struct DevBuf {
+  void* p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+  cudaError_t alloc(size_t n) { return cudaMalloc(&p, n ? n : 16); }
+};
+
+}  // namespace
+
+// ================================================================ C ABI
+extern "C" {
+
+int m3g_abi_version(void) { return 1; }
+
+const char* m3g_last_error(void) { return t_last_error.c_str(); }
+
+uint64_t m3g_launch_count(void) { return g_launches.load(); }
+
+int m3g_set_tuning(const char* key, int64_t value) {
+  if (!key) return fail(M3G_EINVAL, "null key");
+  if (!strcmp(key, "stage_bytes") && value >= 1024) g_tune.stage_bytes = value;
+  else if (!strcmp(key, "ctas_per_sm") && value >= 1 && value <= 8) g_tune.ctas_per_sm = value;
+  else if (!strcmp(key, "max_stages") && value >= 2 && value <= 32) g_tune.max_stages = value;
+  else if (!strcmp(key, "force_generic")) g_tune.force_generic = value != 0;
+  else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
+  return M3G_OK;
+}
+
+int m3g_quant_raw_len(uint32_t dtype, uint64_t n, uint64_t* out_len) {
+  if (!out_len) return fail(M3G_EINVAL, "null out_len");
+  uint64_t v = 0;
+  if (!raw_len_rule(dtype, n, v)) return fail(M3G_ENONE, "no fused kernel for dtype %u, n %llu", dtype,
+                                               static_cast<unsigned long long>(n));
+  *out_len = v;
+  return M3G_OK;
+}
+
+// ---------------------------------------------------------------- host helpers
+// f32_to_bf16_bits (src/quant.rs:186-194): RNE, quiet-NaN guard.
+uint16_t m3g_f32_to_bf16_bits(float x) {
+  uint32_t b;
+  memcpy(&b, &x, 4);
+  const uint32_t bias = 0x7FFFu + ((b >> 16) & 1u);
+  uint16_t bf = static_cast<uint16_t>((b + bias) >> 16);
+  if (std::isnan(x)) bf |= 0x0040u;
+  return bf;
+}
+
+float m3g_bf16_bits_to_f32(uint16_t b) {
+  const uint32_t u = static_cast<uint32_t>(b) << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+}  // extern "C"
+
+namespace {
+// binary32 -> binary16 round-to-nearest-even (the f16 the encoders store).
+uint16_t f32_to_f16_rne(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  const uint16_t sign = static_cast<uint16_t>((x >> 16) & 0x8000u);
+  const uint32_t exp = (x >> 23) & 0xFFu;
+  uint32_t man = x & 0x7FFFFFu;
+  if (exp == 0xFF) return man ? static_cast<uint16_t>(sign | 0x7E00u | (man >> 13)) : (sign | 0x7C00u);
+  const int e = static_cast<int>(exp) - 127 + 15;
+  if (e >= 31) return sign | 0x7C00u;
+  if (e <= 0) {
+    if (e < -10) return sign;
+    man |= 0x800000u;
+    const int shift = 14 - e;
+    uint32_t hm = man >> shift;
+    const uint32_t rb = 1u << (shift - 1), rest = man & ((1u << shift) - 1u);
+    if (rest > rb || (rest == rb && (hm & 1u))) hm += 1;
+    return static_cast<uint16_t>(sign | hm);
+  }
+  const uint32_t hm = man >> 13, rest = man & 0x1FFFu;
+  uint32_t out = (static_cast<uint32_t>(e) << 10) | hm;
+  if (rest > 0x1000u || (rest == 0x1000u && (hm & 1u))) out += 1;
+  return static_cast<uint16_t>(sign | out);
+}
+
+float f16_to_f32_host(uint16_t h) {
+  const uint32_t sign = static_cast<uint32_t>(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1Fu, man = h & 0x3FFu, u;
+  if (exp == 0) {
+    if (man == 0) {
+      u = sign;
+    } else {
+      int e = -1;
+      do { ++e; man <<= 1; } while ((man & 0x400u) == 0);
+      u = sign | (static_cast<uint32_t>(127 - 15 - e) << 23) | ((man & 0x3FFu) << 13);
+    }
+  } else if (exp == 31) {
+    u = sign | 0x7F800000u | (man << 13);
+  } else {
+    u = sign | ((exp + 112u) << 23) | (man << 13);
+  }
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+// Rust `f32 as i32` (saturating, NaN -> 0), then clamp.
+int32_t sat_round_clamp(float v, int32_t lo, int32_t hi) {
+  v = std::round(v);
+  int32_t i;
+  if (std::isnan(v)) i = 0;
+  else if (v >= 2147483647.0f) i = INT32_MAX;
+  else if (v <= -2147483648.0f) i = INT32_MIN;
+  else i = static_cast<int32_t>(v);
+  return i < lo ? lo : (i > hi ? hi : i);
+}
+
+int quantize_block(const float* src, uint64_t src_len, uint8_t* dst, uint64_t dst_len, int qmax, bool q4) {
+  const uint64_t need = q4 ? 18 : 34;
+  if (!src || !dst) return fail(M3G_EINVAL, "null pointer");
+  if (src_len != 32 || dst_len < need) return fail(M3G_ENONE, "needs 32 floats and %llu bytes",
+                                                   static_cast<unsigned long long>(need));
+  float amax = 0.f;
+  for (int i = 0; i < 32; ++i) {
+    if (!std::isfinite(src[i])) return fail(M3G_ENONE, "non-finite input");
+    amax = std::fmax(amax, std::fabs(src[i]));
+  }
+  const uint16_t db = f32_to_f16_rne(amax == 0.f ? 0.f : amax / static_cast<float>(qmax));
+  const float ds = f16_to_f32_host(db);
+  dst[0] = static_cast<uint8_t>(db & 0xFF);
+  dst[1] = static_cast<uint8_t>(db >> 8);
+  if (q4) {
+    if (amax == 0.f) { memset(dst + 2, 0x88, 16); return M3G_OK; }
+    for (int i = 0; i < 16; ++i) {
+      const int32_t lo = sat_round_clamp(src[i] / ds, -8, 7) + 8;
+      const int32_t hi = sat_round_clamp(src[i + 16] / ds, -8, 7) + 8;
+      dst[2 + i] = static_cast<uint8_t>(static_cast<uint8_t>(lo) | static_cast<uint8_t>(hi << 4));
+    }
+  } else {
+    if (amax == 0.f) { memset(dst + 2, 0, 32); return M3G_OK; }
+    for (int i = 0; i < 32; ++i)
+      dst[2 + i] = static_cast<uint8_t>(static_cast<int8_t>(sat_round_clamp(src[i] / ds, -127, 127)));
+  }
+  return M3G_OK;
+}
+}  // namespace
+
+extern "C" {
+
+// quantize_q4_0 (src/quant.rs:206-234).
+int m3g_quantize_q4_0(const float* src, uint64_t src_len, uint8_t* dst, uint64_t dst_len) {
+  return quantize_block(src, src_len, dst, dst_len, 7, true);
+}
+
+// quantize_q8_0 (src/quant.rs:239-264).
+int m3g_quantize_q8_0(const float* src, uint64_t src_len, uint8_t* dst, uint64_t dst_len) {
+  return quantize_block(src, src_len, dst, dst_len, 127, false);
+}
+
+// ---------------------------------------------------------------- decoders
+// dequantize (src/quant.rs:120-173) on the device.
+int m3g_dequantize_dev(const uint8_t* src, uint64_t src_len, uint32_t dtype, float* dst, uint64_t n,
+                       void* stream) {
+  if ((!src && src_len) || (!dst && n)) return fail(M3G_EINVAL, "null pointer");
+  int fmt = -1;
+  uint64_t need = 0;
+  switch (dtype) {
+    case 0: if (src_len < n * 4) return fail(M3G_ENONE, "F32 source too short"); fmt = 0; break;
+    case 1: if (src_len < n * 2) return fail(M3G_ENONE, "F16 source too short"); fmt = 1; break;
+    case 2:
+      if (n % 32) return fail(M3G_ENONE, "Q4_0 needs n %% 32 == 0");
+      if (src_len < n / 32 * 18) return fail(M3G_EPANIC, "Q4_0 source too short (reference assert!)");
+      fmt = 2; break;
+    case 12: case 13:
+      if (n % 256) return fail(M3G_ENONE, "Q4_K needs n %% 256 == 0");
+      if (src_len < n / 256 * 144) return fail(M3G_EPANIC, "Q4_K source too short (reference assert!)");
+      fmt = 12; break;
+    case 14:
+      if (n % 256) return fail(M3G_ENONE, "Q6_K needs n %% 256 == 0");
+      if (src_len < n / 256 * 210) return fail(M3G_ENONE, "Q6_K source too short");
+      fmt = 14; break;
+    case 8:
+      if (n % 32) return fail(M3G_ENONE, "Q8_0 needs n %% 32 == 0");
+      if (src_len < n / 32 * 34) return fail(M3G_ENONE, "Q8_0 source too short");
+      fmt = 8; break;
+    default:
+      return fail(M3G_ENONE, "dequantize: unsupported dtype %u", dtype);
+  }
+  (void)need;
+  if (n == 0) return M3G_OK;
+  DevState* ds = nullptr;
+  if (int rc = current_dev_state(&ds)) return rc;
+  const long long units = (fmt <= 1) ? static_cast<long long>(n) : static_cast<long long>(n) / (fmt == 12 || fmt == 14 ? 256 : 32) * 32;
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((units + 255) / 256, 16ll * ds->sms)));
+  cudaError_t e = m3g::launch_dequant(fmt, src, dst, static_cast<long long>(n), grid, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "k_dequant launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return M3G_OK;
+}
+
+int m3g_dequantize(const uint8_t* src, uint64_t src_len, uint32_t dtype, float* dst, uint64_t n) {
+  if ((!src && src_len) || (!dst && n)) return fail(M3G_EINVAL, "null pointer");
+  DevState* ds = nullptr;
+  if (int rc = current_dev_state(&ds)) return rc;
+  DevBuf ds_src, ds_dst;
+  M3G_CUDA(ds_src.alloc(src_len));
+  M3G_CUDA(ds_dst.alloc(n * sizeof(float)));
+  if (src_len) M3G_CUDA(cudaMemcpy(ds_src.p, src, src_len, cudaMemcpyHostToDevice));
+  int rc = m3g_dequantize_dev(static_cast<const uint8_t*>(ds_src.p), src_len, dtype, static_cast<float*>(ds_dst.p),
+                              n, nullptr);
+  if (rc) return rc;
+  if (n) M3G_CUDA(cudaMemcpy(dst, ds_dst.p, n * sizeof(float), cudaMemcpyDeviceToHost));
+  return M3G_OK;
+}
+
+// ---------------------------------------------------------------- fused GEMV
+int m3g_matvec_quant_dev(const float* x, const uint8_t* raw, uint64_t raw_len, uint32_t dtype, uint64_t in_dim,
+                         uint64_t out_dim, uint64_t batch, float* y, void* stream) {
+  FmtInfo f;
+  if (int rc = gemv_rules(dtype, raw_len, in_dim, out_dim, f)) return rc;
+  if (!x || !raw || !y) return fail(M3G_EINVAL, "null pointer");
+  if (batch == 0) return M3G_OK;
+  DevState* ds = nullptr;
+  if (int rc = current_dev_state(&ds)) return rc;
+  return gemv_batch_launch(*ds, f, raw, x, y, static_cast<long long>(in_dim), static_cast<long long>(out_dim),
+                           static_cast<long long>(batch), static_cast<cudaStream_t>(stream));
+}
+
+// matvec_quant (src/matvec_quant.rs:87-109) with host buffers.
+int m3g_matvec_quant(const float* x, uint64_t x_len, const uint8_t* raw, uint64_t raw_len, uint32_t dtype,
+                     uint64_t in_dim, uint64_t out_dim, float* y) {
+  if (x_len != in_dim) return fail(M3G_ENONE, "x has %llu elements, in_dim is %llu",
+                                   static_cast<unsigned long long>(x_len), static_cast<unsigned long long>(in_dim));
+  FmtInfo f;
+  if (int rc = gemv_rules(dtype, raw_len, in_dim, out_dim, f)) return rc;
+  if (!x || !raw || !y) return fail(M3G_EINVAL, "null pointer");
+  DevState* ds = nullptr;
+  if (int rc = current_dev_state(&ds)) return rc;
+  uint64_t need = 0;
+  raw_len_rule(dtype, in_dim * out_dim, need);
+  DevBuf dw, dx, dy;
+  M3G_CUDA(dw.alloc(need));
+  M3G_CUDA(dx.alloc(in_dim * sizeof(float)));
+  M3G_CUDA(dy.alloc(out_dim * sizeof(float)));
+  M3G_CUDA(cudaMemcpy(dw.p, raw, need, cudaMemcpyHostToDevice));
+  M3G_CUDA(cudaMemcpy(dx.p, x, in_dim * sizeof(float), cudaMemcpyHostToDevice));
+  if (int rc = gemv_launch(*ds, f, static_cast<const uint8_t*>(dw.p), static_cast<const float*>(dx.p),
+                           static_cast<float*>(dy.p), static_cast<long long>(in_dim),
+                           static_cast<long long>(out_dim), nullptr))
+    return rc;
+  M3G_CUDA(cudaMemcpy(y, dy.p, out_dim * sizeof(float), cudaMemcpyDeviceToHost));
+  return check_status(*ds);
+}
+
+int m3g_device_status(int device, uint32_t* out, int clear) {
+  DevState* ds = nullptr;
+  if (int rc = dev_state(device, &ds)) return rc;
+  int prev = 0;
+  M3G_CUDA(cudaGetDevice(&prev));
+  M3G_CUDA(cudaSetDevice(device));
+  uint32_t s = 0;
+  cudaError_t e = cudaMemcpy(&s, ds->status, sizeof s, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear) e = cudaMemset(ds->status, 0, sizeof s);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "m3g_device_status");
+  if (out) *out = s;
+  return M3G_OK;
+}
+
+}  // extern "C"
+
+// ================================================================ offload context
+struct ResidentTensor {
+  uint32_t dtype = 0;
+  uint64_t in_dim = 0, out_dim = 0, raw_len = 0;
+  uint8_t* d_raw = nullptr;
+};
+
+struct m3g_offload {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint64_t max_in = 0, max_out = 0;
+  uint64_t cap_batch = 0;
+  float* d_x = nullptr;
+  float* d_y = nullptr;
+  float* h_x = nullptr;  // pinned staging
+  float* h_y = nullptr;
+  uint32_t* h_status = nullptr;
+  uint64_t calls = 0;
+  std::unordered_map<uint64_t, ResidentTensor> tensors;
+};
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+void free_io(m3g_offload* c) {
+  if (c->d_x) cudaFree(c->d_x);
+  if (c->d_y) cudaFree(c->d_y);
+  if (c->h_x) cudaFreeHost(c->h_x);
+  if (c->h_y) cudaFreeHost(c->h_y);
+  if (c->h_status) cudaFreeHost(c->h_status);
+  c->d_x = c->d_y = c->h_x = c->h_y = nullptr;
+  c->h_status = nullptr;
+  c->cap_batch = 0;
+}
+
+int ensure_io(m3g_offload* c, uint64_t batch) {
+  if (batch <= c->cap_batch) return M3G_OK;
+  free_io(c);
+  const size_t nx = static_cast<size_t>(std::max<uint64_t>(c->max_in, 16) * batch);
+  const size_t ny = static_cast<size_t>(std::max<uint64_t>(c->max_out, 16) * batch);
+  M3G_CUDA(cudaMalloc(&c->d_x, nx * sizeof(float)));
+  M3G_CUDA(cudaMalloc(&c->d_y, ny * sizeof(float)));
+  M3G_CUDA(cudaMallocHost(&c->h_x, nx * sizeof(float)));
+  M3G_CUDA(cudaMallocHost(&c->h_y, ny * sizeof(float)));
+  M3G_CUDA(cudaMallocHost(&c->h_status, 16));
+  c->cap_batch = batch;
+  return M3G_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+// GpuOffload::try_new (src/inference_gpu.rs:58-127).
+int m3g_offload_create(int device, uint64_t max_in, uint64_t max_out, m3g_offload** out) {
+  if (!out) return fail(M3G_EINVAL, "null out");
+  *out = nullptr;
+  DevState* ds = nullptr;
+  if (int rc = dev_state(device, &ds)) return rc;
+  DeviceGuard g(device);
+  auto* c = new m3g_offload();
+  c->device = device;
+  c->max_in = max_in;
+  c->max_out = max_out;
+  cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete c;
+    return cuda_fail(e, "cudaStreamCreate");
+  }
+  if (int rc = ensure_io(c, 1)) {
+    free_io(c);
+    cudaStreamDestroy(c->stream);
+    delete c;
+    return rc;
+  }
+  *out = c;
+  return M3G_OK;
+}
+
+void m3g_offload_destroy(m3g_offload* c) {
+  if (!c) return;
+  DeviceGuard g(c->device);
+  cudaStreamSynchronize(c->stream);
+  for (auto& kv : c->tensors) cudaFree(kv.second.d_raw);
+  free_io(c);
+  cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+// GpuOffload::upload (src/inference_gpu.rs:131-177).
+int m3g_offload_upload(m3g_offload* c, uint64_t tidx, uint32_t dtype, const uint8_t* raw, uint64_t raw_len,
+                       uint64_t in_dim, uint64_t out_dim) {
+  if (!c) return fail(M3G_EINVAL, "null context");
+  FmtInfo f;
+  if (!fmt_info(dtype, f)) return fail(M3G_ENONE, "upload: dtype %u has no fused kernel", dtype);
+  if (in_dim == 0 || out_dim == 0) return fail(M3G_ENONE, "upload: zero dimension");
+  if (in_dim > (1ull << 31) || out_dim > (1ull << 31)) return fail(M3G_EINVAL, "upload: dimension too large");
+  uint64_t expect = 0;
+  if (!raw_len_rule(dtype, in_dim * out_dim, expect) || expect != raw_len)
+    return fail(M3G_ENONE, "upload: raw_len %llu != quant_raw_len %llu", static_cast<unsigned long long>(raw_len),
+                static_cast<unsigned long long>(expect));
+  if (!raw) return fail(M3G_EINVAL, "null raw");
+  DeviceGuard g(c->device);
+  ResidentTensor t;
+  t.dtype = dtype;
+  t.in_dim = in_dim;
+  t.out_dim = out_dim;
+  t.raw_len = raw_len;
+  M3G_CUDA(cudaMalloc(&t.d_raw, raw_len + 16));
+  cudaError_t e = cudaMemcpy(t.d_raw, raw, raw_len, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(t.d_raw);
+    return cuda_fail(e, "upload copy");
+  }
+  auto it = c->tensors.find(tidx);
+  if (it != c->tensors.end()) {
+    cudaStreamSynchronize(c->stream);
+    cudaFree(it->second.d_raw);
+    it->second = t;
+  } else {
+    c->tensors.emplace(tidx, t);
+  }
+  return M3G_OK;
+}
+
+int m3g_offload_offloaded(const m3g_offload* c, uint64_t tidx) { return c && c->tensors.count(tidx) ? 1 : 0; }
+
+uint64_t m3g_offload_tensor_count(const m3g_offload* c) { return c ? c->tensors.size() : 0; }
+
+uint64_t m3g_offload_calls(const m3g_offload* c) { return c ? c->calls : 0; }
+
+const uint8_t* m3g_offload_tensor_ptr(const m3g_offload* c, uint64_t tidx) {
+  if (!c) return nullptr;
+  auto it = c->tensors.find(tidx);
+  return it == c->tensors.end() ? nullptr : it->second.d_raw;
+}
+
+int m3g_offload_matvec_dev(m3g_offload* c, uint64_t tidx, const float* x, uint64_t batch, float* y, void* stream) {
+  if (!c) return fail(M3G_EINVAL, "null context");
+  auto it = c->tensors.find(tidx);
+  if (it == c->tensors.end()) return fail(M3G_ENOTFOUND, "tensor %llu not resident", static_cast<unsigned long long>(tidx));
+  if (!x || !y) return fail(M3G_EINVAL, "null pointer");
+  const ResidentTensor& t = it->second;
+  FmtInfo f;
+  fmt_info(t.dtype, f);
+  DevState* ds = nullptr;
+  if (int rc = dev_state(c->device, &ds)) return rc;
+  DeviceGuard g(c->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  int rc = gemv_batch_launch(*ds, f, t.d_raw, x, y, static_cast<long long>(t.in_dim),
+                             static_cast<long long>(t.out_dim), static_cast<long long>(batch), st);
+  if (!rc) ++c->calls;
+  return rc;
+}
+
+// GpuOffload::matvec (src/inference_gpu.rs:188-237), host x and y, batched.
+int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint64_t batch, uint64_t in_dim,
+                             uint64_t out_dim, float* y) {
+  if (!c) return fail(M3G_EINVAL, "null context");
+  auto it = c->tensors.find(tidx);
+  if (it == c->tensors.end()) return fail(M3G_ENOTFOUND, "tensor %llu not resident", static_cast<unsigned long long>(tidx));
+  const ResidentTensor& t = it->second;
+  if (t.in_dim != in_dim || t.out_dim != out_dim)
+    return fail(M3G_ENONE, "matvec dims %llux%llu differ from upload %llux%llu",
+                static_cast<unsigned long long>(in_dim), static_cast<unsigned long long>(out_dim),
+                static_cast<unsigned long long>(t.in_dim), static_cast<unsigned long long>(t.out_dim));
+  if (in_dim > c->max_in || out_dim > c->max_out) return fail(M3G_ENONE, "matvec exceeds max_in/max_out");
+  if (!x || !y) return fail(M3G_EINVAL, "null pointer");
+  if (batch == 0) return M3G_OK;
+  DeviceGuard g(c->device);
+  if (int rc = ensure_io(c, batch)) return rc;
+  const size_t bx = static_cast<size_t>(in_dim * batch) * sizeof(float);
+  const size_t by = static_cast<size_t>(out_dim * batch) * sizeof(float);
+  memcpy(c->h_x, x, bx);
+  M3G_CUDA(cudaMemcpyAsync(c->d_x, c->h_x, bx, cudaMemcpyHostToDevice, c->stream));
+  if (int rc = m3g_offload_matvec_dev(c, tidx, c->d_x, batch, c->d_y, c->stream)) return rc;
+  DevState* ds = nullptr;
+  if (int rc = dev_state(c->device, &ds)) return rc;
+  M3G_CUDA(cudaMemcpyAsync(c->h_y, c->d_y, by, cudaMemcpyDeviceToHost, c->stream));
+  M3G_CUDA(cudaMemcpyAsync(c->h_status, ds->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+  M3G_CUDA(cudaStreamSynchronize(c->stream));
+  memcpy(y, c->h_y, by);
+  if (*c->h_status & m3g::kStatusCopyTimeout) {
+    cudaMemset(ds->status, 0, sizeof(uint32_t));
+    return fail(M3G_ETIMEOUT, "a staged weight copy did not complete in time");
+  }
+  return M3G_OK;
+}
+
+int m3g_offload_matvec(m3g_offload* c, uint64_t tidx, const float* x, uint64_t in_dim, uint64_t out_dim,
+                       float* y) {
+  return m3g_offload_matvec_batch(c, tidx, x, 1, in_dim, out_dim, y);
+}
+
+}  // extern "C"

@@ -1,0 +1,256 @@
+// m3g_kernels.cu -- sm_100a kernels of the fused dequantise-and-matvec path.
+//
+// k_gemv_stream<F, UPT>   the fast path: whole rows of GGUF blocks stream from
+//                         HBM into a ring of shared-memory stages by 1-D TMA
+//                         bulk copies (one elected thread, mbarrier
+//                         completion), while every thread decodes its fixed
+//                         units of each staged row against x held in
+//                         registers; rows reduce with warp shuffles.
+// k_gemv_generic<F>       any shape, including blocks that straddle two
+//                         output rows (in_dim not a multiple of the block):
+//                         one warp per block, exact decode, atomics per row.
+// k_dequant<...>          bit-exact block decode to f32 (src/quant.rs:9-173).
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "m3g_device.cuh"
+#include "m3g_formats.cuh"
+#include "m3g_internal.h"
+
+namespace m3g {
+
+// Copy-wait limit of the staged pipeline: a stage normally lands within
+// microseconds; after this long the kernel reports kStatusCopyTimeout.
+constexpr uint64_t kCopyTimeoutNs = 2000000000ull;
+
+template <class F, int UPT>
+__global__ void __launch_bounds__(256) k_gemv_stream(const StreamArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x;
+  const int slot = tid / a.TS;
+  const int ls = tid - slot * a.TS;
+  const int lane = tid & 31;
+  const int wis = ls >> 5;
+  const int WPS = a.TS >> 5;
+
+  const long long row0 = static_cast<long long>(blockIdx.x) * a.rows_per_cta;
+  long long row_end = row0 + a.rows_per_cta;
+  if (row_end > a.rows) row_end = a.rows;
+  if (row0 >= row_end) return;
+  const int nrows = static_cast<int>(row_end - row0);
+  const int nst = (nrows + a.R - 1) / a.R;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(a.NS) * a.stage_stride);
+  float* red = reinterpret_cast<float*>(bars + a.NS);
+
+  // x of this thread's units, resident in registers for the whole kernel.
+  float xr[UPT][F::kUnitElems];
+  float xe[UPT][F::kExtra];
+  bool act[UPT];
+#pragma unroll
+  for (int k = 0; k < UPT; ++k) {
+    const int u = ls + k * a.TS;
+    act[k] = u < a.U;
+#pragma unroll
+    for (int i = 0; i < F::kUnitElems; ++i) xr[k][i] = act[k] ? __ldg(a.x + F::xpos(u, i)) : 0.f;
+    F::prep(xr[k], xe[k]);
+  }
+
+  const uint8_t* wbase = a.w + row0 * static_cast<long long>(a.RB);
+  uint64_t policy = 0;
+  if (tid == 0) {
+    for (int s = 0; s < a.NS; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+    policy = l2_evict_first_policy();
+  }
+  __syncthreads();
+
+  auto issue = [&](int s) {
+    const int rows_s = min(a.R, nrows - s * a.R);
+    const uint32_t bytes = static_cast<uint32_t>(rows_s) * static_cast<uint32_t>(a.RB);
+    uint64_t* bar = &bars[s % a.NS];
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_g2s(smem + static_cast<size_t>(s % a.NS) * a.stage_stride,
+             wbase + static_cast<long long>(s) * a.R * a.RB, bytes, bar, policy);
+  };
+  if (tid == 0) {
+    const int pre = min(a.NS, nst);
+    for (int s = 0; s < pre; ++s) issue(s);
+  }
+
+  for (int i = 0; i < nst; ++i) {
+    const int buf = i % a.NS;
+    const uint32_t par = static_cast<uint32_t>(i / a.NS) & 1u;
+    const bool ok = mbar_wait_bounded(&bars[buf], par, kCopyTimeoutNs);
+    const uint8_t* sb = smem + static_cast<size_t>(buf) * a.stage_stride;
+    const int rows_here = min(a.R, nrows - i * a.R);
+    float* redb = red + (i & 1) * a.R * WPS;
+    for (int rr = slot; rr < a.R; rr += a.RPI) {
+      float acc = 0.f;
+      if (ok && rr < rows_here) {
+        const uint8_t* rowp = sb + static_cast<size_t>(rr) * a.RB;
+#pragma unroll
+        for (int k = 0; k < UPT; ++k)
+          if (act[k]) acc += F::dot(rowp, ls + k * a.TS, xr[k], xe[k]);
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) redb[rr * WPS + wis] = acc;
+    }
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        atomicOr(a.status, kStatusCopyTimeout);
+        // Let the copies still in flight land (bounded) before the CTA exits.
+        const int last = min(nst, i + a.NS);
+        for (int s = i; s < last; ++s)
+          (void)mbar_wait_bounded(&bars[s % a.NS], static_cast<uint32_t>(s / a.NS) & 1u, kCopyTimeoutNs);
+      }
+      return;
+    }
+    if (tid == 0 && i + a.NS < nst) {
+      fence_proxy_async_smem();
+      issue(i + a.NS);
+    }
+    if (tid < rows_here) {
+      float s = 0.f;
+      for (int w = 0; w < WPS; ++w) s += redb[tid * WPS + w];
+      a.y[row0 + static_cast<long long>(i) * a.R + tid] = s;
+    }
+  }
+}
+
+// Generic fallback: one warp per block, lane e-slices decode exactly, each
+// block's products are reduced per output row it overlaps and added with one
+// atomic per (block, row).  y must be zeroed first.
+template <int FMT>
+__device__ __forceinline__ float elem(const uint8_t* blk, int e) {
+  if constexpr (FMT == 12) return q4k_elem(blk, e);
+  else if constexpr (FMT == 14) return q6k_elem(blk, e);
+  else if constexpr (FMT == 8) return q8_0_elem(blk, e);
+  else return q4_0_elem(blk, e);
+}
+
+template <int FMT, int BE, int BB>
+__global__ void __launch_bounds__(256) k_gemv_generic(const uint8_t* __restrict__ w, const float* __restrict__ x,
+                                                      float* __restrict__ y, long long in_dim, long long nblocks) {
+  constexpr int EPL = BE / 32;  // elements per lane
+  const int lane = threadIdx.x & 31;
+  const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  for (long long b = warp; b < nblocks; b += nwarps) {
+    const uint8_t* blk = w + b * BB;
+    const long long base = b * BE;
+    const long long j0 = base / in_dim;
+    const long long j_last = (base + BE - 1) / in_dim;
+    float v[EPL];
+    int rel[EPL];
+#pragma unroll
+    for (int t = 0; t < EPL; ++t) {
+      const int e = lane * EPL + t;
+      const long long k = base + e;
+      const long long j = k / in_dim;
+      v[t] = elem<FMT>(blk, e) * __ldg(x + (k - j * in_dim));
+      rel[t] = static_cast<int>(j - j0);
+    }
+    for (long long r = 0; r <= j_last - j0; ++r) {
+      float s = 0.f;
+#pragma unroll
+      for (int t = 0; t < EPL; ++t)
+        if (rel[t] == r) s += v[t];
+      s = warp_sum(s);
+      if (lane == 0) atomicAdd(y + j0 + r, s);
+    }
+  }
+}
+
+template <int FMT, int BE, int BB>
+__global__ void __launch_bounds__(256) k_dequant(const uint8_t* __restrict__ w, float* __restrict__ out,
+                                                 long long nblocks) {
+  constexpr int EPL = BE / 32;
+  const int lane = threadIdx.x & 31;
+  const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  for (long long b = warp; b < nblocks; b += nwarps) {
+    const uint8_t* blk = w + b * BB;
+#pragma unroll
+    for (int t = 0; t < EPL; ++t) {
+      const int e = t * 32 + lane;  // coalesced stores
+      out[b * BE + e] = elem<FMT>(blk, e);
+    }
+  }
+}
+
+__global__ void k_dequant_f32(const uint8_t* __restrict__ w, float* __restrict__ out, long long n) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const uint8_t* p = w + 4 * i;
+    out[i] = __uint_as_float(static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8) |
+                             (static_cast<uint32_t>(p[2]) << 16) | (static_cast<uint32_t>(p[3]) << 24));
+  }
+}
+
+__global__ void k_dequant_f16(const uint8_t* __restrict__ w, float* __restrict__ out, long long n) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    out[i] = f16_to_f32(static_cast<uint32_t>(w[2 * i]) | (static_cast<uint32_t>(w[2 * i + 1]) << 8));
+  }
+}
+
+// ---------------------------------------------------------------- launchers
+
+template <class F>
+static cudaError_t launch_stream_fmt(const StreamArgs& a, int threads, int grid, size_t smem, int upt,
+                                     cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  switch (upt) {
+    case 1:
+      e = cudaFuncSetAttribute(k_gemv_stream<F, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess) k_gemv_stream<F, 1><<<grid, threads, smem, st>>>(a);
+      break;
+    case 2:
+      e = cudaFuncSetAttribute(k_gemv_stream<F, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess) k_gemv_stream<F, 2><<<grid, threads, smem, st>>>(a);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_stream(int fmt, const StreamArgs& a, int threads, int grid, size_t smem, int upt,
+                               cudaStream_t st) {
+  switch (fmt) {
+    case 12: return launch_stream_fmt<FmtQ4K>(a, threads, grid, smem, upt, st);
+    case 14: return launch_stream_fmt<FmtQ6K>(a, threads, grid, smem, upt, st);
+    case 8: return launch_stream_fmt<FmtQ80>(a, threads, grid, smem, upt, st);
+    case 2: return launch_stream_fmt<FmtQ40>(a, threads, grid, smem, upt, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float* y, long long in_dim,
+                                long long nblocks, int grid, cudaStream_t st) {
+  switch (fmt) {
+    case 12: k_gemv_generic<12, 256, 144><<<grid, 256, 0, st>>>(w, x, y, in_dim, nblocks); break;
+    case 14: k_gemv_generic<14, 256, 210><<<grid, 256, 0, st>>>(w, x, y, in_dim, nblocks); break;
+    case 8: k_gemv_generic<8, 32, 34><<<grid, 256, 0, st>>>(w, x, y, in_dim, nblocks); break;
+    case 2: k_gemv_generic<2, 32, 18><<<grid, 256, 0, st>>>(w, x, y, in_dim, nblocks); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant(int fmt, const uint8_t* w, float* out, long long n_elems, int grid, cudaStream_t st) {
+  switch (fmt) {
+    case 0: k_dequant_f32<<<grid, 256, 0, st>>>(w, out, n_elems); break;
+    case 1: k_dequant_f16<<<grid, 256, 0, st>>>(w, out, n_elems); break;
+    case 12: k_dequant<12, 256, 144><<<grid, 256, 0, st>>>(w, out, n_elems / 256); break;
+    case 14: k_dequant<14, 256, 210><<<grid, 256, 0, st>>>(w, out, n_elems / 256); break;
+    case 8: k_dequant<8, 32, 34><<<grid, 256, 0, st>>>(w, out, n_elems / 32); break;
+    case 2: k_dequant<2, 32, 18><<<grid, 256, 0, st>>>(w, out, n_elems / 32); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace m3g

@@ -1,0 +1,105 @@
+"""Fused dequantise-and-matvec with the API of m3_avm's src/matvec_quant.rs.
+
+``matvec_quant`` keeps the reference's ``Option`` contract: ``None`` for an
+unsupported dtype, zero dims, ``len(x) != in_dim`` or a short ``raw``; every
+other call runs the sm_100a kernels of ``libm3gemv.so``.  Weights are GGUF
+bytes with K = in_dim fastest: y[j] = sum_i x[i] * W[i + j*in_dim].
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+
+
+def _u8(a) -> np.ndarray:
+    if isinstance(a, (bytes, bytearray, memoryview)):
+        return np.frombuffer(bytes(a), np.uint8)
+    return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+def quant_raw_len(dtype: int, n: int):
+    """src/matvec_quant.rs:51-83: bytes for n elements, or None."""
+    out = ctypes.c_uint64()
+    rc = _lib.load().m3g_quant_raw_len(dtype, n, ctypes.byref(out))
+    return out.value if rc == _lib.M3G_OK else None
+
+
+def matvec_quant(x, raw, dtype: int, in_dim: int, out_dim: int):
+    """src/matvec_quant.rs:87-109: Some(y) as a float32 array, or None."""
+    xa = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    r = _u8(raw)
+    y = np.empty(max(out_dim, 1), np.float32)
+    rc = _lib.load().m3g_matvec_quant(xa.ctypes.data, xa.size, r.ctypes.data, r.size, dtype, in_dim, out_dim,
+                                      y.ctypes.data)
+    if rc == _lib.M3G_ENONE:
+        return None
+    _lib.check(rc)
+    return y[:out_dim]
+
+
+def _direct(x, raw, dtype: int, in_dim: int, out_dim: int) -> np.ndarray:
+    # The reference's direct kernels index raw without checks and panic on a
+    # short slice; the mirror raises instead.
+    y = matvec_quant(x, raw, dtype, in_dim, out_dim)
+    if y is None:
+        raise IndexError(_lib.last_error())
+    return y
+
+
+def matvec_q4k(x, raw, in_dim: int, out_dim: int) -> np.ndarray:
+    """src/matvec_quant.rs:221-223."""
+    return _direct(x, raw, 12, in_dim, out_dim)
+
+
+def matvec_q4k_impl(x, raw, in_dim: int, out_dim: int, use_avx2: bool) -> np.ndarray:
+    """src/matvec_quant.rs:228-243; the SIMD selector has no meaning on the GPU."""
+    del use_avx2
+    return _direct(x, raw, 12, in_dim, out_dim)
+
+
+def matvec_q6k(x, raw, in_dim: int, out_dim: int) -> np.ndarray:
+    """src/matvec_quant.rs:361-365."""
+    return _direct(x, raw, 14, in_dim, out_dim)
+
+
+def matvec_q4_0(x, raw, in_dim: int, out_dim: int) -> np.ndarray:
+    """src/matvec_quant.rs:368-372."""
+    return _direct(x, raw, 2, in_dim, out_dim)
+
+
+def matvec_q8_0(x, raw, in_dim: int, out_dim: int) -> np.ndarray:
+    """src/matvec_quant.rs:375-382."""
+    return _direct(x, raw, 8, in_dim, out_dim)
+
+
+def matvec_quant_dev(x, raw, dtype: int, in_dim: int, out_dim: int, y=None, stream=None):
+    """Device form over CUDA tensors: x is (in_dim,) or (batch, in_dim) float32,
+    raw a uint8 tensor of GGUF bytes; returns y of shape (out_dim,) or (batch, out_dim)."""
+    import torch
+
+    batch = 1 if x.dim() == 1 else x.shape[0]
+    if y is None:
+        shape = (out_dim,) if x.dim() == 1 else (batch, out_dim)
+        y = torch.empty(shape, dtype=torch.float32, device=x.device)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+    rc = _lib.load().m3g_matvec_quant_dev(x.data_ptr(), raw.data_ptr(), raw.numel(), dtype, in_dim, out_dim, batch,
+                                          y.data_ptr(), ctypes.c_void_p(st))
+    _lib.check(rc)
+    return y
+
+
+def set_tuning(key: str, value: int) -> None:
+    _lib.check(_lib.load().m3g_set_tuning(key.encode(), int(value)))
+
+
+def launch_count() -> int:
+    return int(_lib.load().m3g_launch_count())
+
+
+def device_status(device: int = 0, clear: bool = False) -> int:
+    out = ctypes.c_uint32()
+    _lib.check(_lib.load().m3g_device_status(device, ctypes.byref(out), int(clear)))
+    return out.value
