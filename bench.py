@@ -219,16 +219,43 @@ def run_ours(args) -> int:
     y = torch.empty(OUT_DIM, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step(i):
-        g.matvec_dev(i % n_copies, x, y, stream=stream.cuda_stream)
+    def step(i, st):
+        g.matvec_dev(i % n_copies, x, y, stream=st.cuda_stream)
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for i in range(args.warmup):
-        step(i)
+    # The timed steps replay CUDA graphs that hold one launch per weight copy,
+    # so the host's launch cost does not gate the GPU.
+    cap = torch.cuda.Stream(dev)
+    graphs = []
+    if not args.no_graph:
+        for n_launch in sorted({n_copies, args.steps % n_copies} - {0}, reverse=True):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=cap, capture_error_mode="thread_local"):
+                for c in range(n_launch):
+                    step(c, cap)
+            graphs.append((n_launch, gr))
+    gmap = dict(graphs)
+
+    def run_steps(k):
+        if args.no_graph:
+            for i in range(k):
+                step(i, stream)
+            return
+        full, rest = divmod(k, n_copies)
+        for _ in range(full):
+            gmap[n_copies].replay()
+        if rest:
+            if rest not in gmap:
+                for i in range(rest):
+                    step(i, stream)
+            else:
+                gmap[rest].replay()
+
+    run_steps(args.warmup)
     barrier()
     sampler = ClockSampler(local)
     sampler.start()
@@ -238,11 +265,11 @@ def run_ours(args) -> int:
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for i in range(args.steps):
-        step(i)
+    run_steps(args.steps)
     ev1.record(stream)
     torch.cuda.synchronize(dev)
-    launches = int(lib.m3g_launch_count()) - launches0
+    host_launches = int(lib.m3g_launch_count()) - launches0
+    launches = args.steps if not args.no_graph else host_launches
     ms = ev0.elapsed_time(ev1)
     barrier()
     clocks = sampler.stop()
@@ -256,7 +283,7 @@ def run_ours(args) -> int:
 
     # e2e: host x -> device, GEMV, device y -> host, through the C ABI offload call.
     xh = synth.activations(IN_DIM, seed=2)
-    e2e_steps = min(args.steps, 5000)
+    e2e_steps = 0 if args.no_e2e else min(args.steps, 5000)
     for i in range(min(args.warmup, 50)):
         g.matvec(i % n_copies, xh, IN_DIM, OUT_DIM)
     barrier()
@@ -264,7 +291,7 @@ def run_ours(args) -> int:
     for i in range(e2e_steps):
         if g.matvec(i % n_copies, xh, IN_DIM, OUT_DIM) is None:
             raise RuntimeError("offload matvec failed: " + _lib.last_error())
-    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    e2e_s = (time.perf_counter() - t0) / max(e2e_steps, 1)
     te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
@@ -302,6 +329,8 @@ def run_ours(args) -> int:
                     "d2h_bytes_per_step": 4 * OUT_DIM, "us_per_call": round(float(te.item()) * 1e6, 2),
                     "api": "m3g_offload_matvec (host x/y, resident weights)"},
             "gpu_launches": launches,
+            "timing": "CUDA events around CUDA-graph replays of the GEMV launches" if not args.no_graph
+                      else "CUDA events around host-launched GEMVs",
             "clocks": clocks,
             "device_status": status,
         }
@@ -328,6 +357,8 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-graph", action="store_true", help="launch each step from the host instead of a CUDA graph")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

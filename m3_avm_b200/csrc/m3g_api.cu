@@ -77,6 +77,9 @@ struct Tuning {
   int64_t ctas_per_sm = 2;
   int64_t max_stages = 8;
   int64_t force_generic = 0;    // route every GEMV through the generic kernel (parity tests)
+  int64_t pdl = 1;              // programmatic dependent launch of the streaming kernels
+  int64_t mma = 1;              // tensor-core GEMV where the shape allows it
+  int64_t mma_stages = 4;       // pipeline stages of the tensor-core GEMV
 };
 Tuning g_tune;
 
@@ -91,13 +94,18 @@ struct DevState {
 std::mutex g_dev_mu;
 std::vector<DevState> g_dev;
 
+int g_ndev = -1;
+
 int dev_state(int device, DevState** out) {
   std::lock_guard<std::mutex> lk(g_dev_mu);
-  int n = 0;
-  cudaError_t e = cudaGetDeviceCount(&n);
-  if (e != cudaSuccess || n <= 0) return fail(M3G_ECUDA, "no CUDA device: %s", cudaGetErrorString(e));
-  if (device < 0 || device >= n) return fail(M3G_EINVAL, "device %d out of range [0,%d)", device, n);
-  if (static_cast<int>(g_dev.size()) < n) g_dev.resize(n);
+  if (g_ndev <= 0) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n <= 0) return fail(M3G_ECUDA, "no CUDA device: %s", cudaGetErrorString(e));
+    g_ndev = n;
+    g_dev.resize(n);
+  }
+  if (device < 0 || device >= g_ndev) return fail(M3G_EINVAL, "device %d out of range [0,%d)", device, g_ndev);
   DevState& d = g_dev[device];
   if (!d.ready) {
     int prev = 0;
@@ -131,12 +139,12 @@ struct StreamPlan {
   size_t smem = 0;
 };
 
-bool plan_stream(const FmtInfo& f, long long in_dim, long long rows, const uint8_t* w, const DevState& ds,
-                 StreamPlan& p) {
+bool plan_stream(const FmtInfo& f, long long in_dim, long long rows, const uint8_t* w, const float* x,
+                 const DevState& ds, StreamPlan& p) {
   if (g_tune.force_generic) return false;
   if (in_dim % f.be) return false;  // blocks straddle rows
   const long long RB = (in_dim / f.be) * f.bb;
-  if (RB % 16 || reinterpret_cast<uintptr_t>(w) % 16) return false;
+  if (RB % 16 || reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16) return false;
   if (RB > (1 << 20) || rows > (1ll << 31) - 1) return false;
   const long long U = in_dim / f.unit_elems;
   int upt = 0, TS = 0;
@@ -147,50 +155,126 @@ bool plan_stream(const FmtInfo& f, long long in_dim, long long rows, const uint8
   }
   if (!upt) return false;
   const int RPI = std::max(1, 256 / TS);
-  const int threads = TS * RPI;
   const int WPS = TS / 32;
   const long long ctas_per_sm = std::max<int64_t>(1, g_tune.ctas_per_sm);
-  const long long budget =
-      std::min<long long>(ds.smem_optin, ds.smem_per_sm / ctas_per_sm - 1024);
+  const long long budget = std::min<long long>(ds.smem_optin, ds.smem_per_sm / ctas_per_sm - 1024);
+  const long long x_bytes = 4 * in_dim;
+  bool stage_x = x_bytes <= budget / 3;
   long long m = std::max<long long>(1, std::min<long long>(TS, g_tune.stage_bytes / (RPI * RB)));
-  for (;; --m) {
+  for (;;) {
     const long long R = RPI * m;
     const long long stride = (R * RB + 16 + 127) / 128 * 128;
-    const long long red = 2 * R * WPS * 4;
-    long long NS = std::min<long long>(g_tune.max_stages, (budget - red - 8 * g_tune.max_stages) / stride);
+    const long long xb = stage_x ? (x_bytes + 127) / 128 * 128 : 0;
+    const long long per_stage_fixed = stride + R * WPS * 4 + 16;
+    long long NS = std::min<long long>(g_tune.max_stages, (budget - xb - 16) / per_stage_fixed);
     if (NS >= 2) {
       p.a.R = static_cast<int>(R);
       p.a.NS = static_cast<int>(NS);
       p.a.stage_stride = static_cast<int>(stride);
-      p.smem = static_cast<size_t>(NS * stride + 8 * NS + red);
+      p.a.stage_x = stage_x ? 1 : 0;
+      p.a.off_x = static_cast<int>(NS * stride);
+      p.a.off_red = static_cast<int>(NS * stride + xb);
+      p.a.off_bar = static_cast<int>((p.a.off_red + NS * R * WPS * 4 + 15) / 16 * 16);
+      p.smem = static_cast<size_t>(p.a.off_bar + 16 * NS + 16);
       break;
     }
-    if (m == 1) return false;
+    if (m > 1) { --m; continue; }
+    if (stage_x) { stage_x = false; continue; }
+    return false;
   }
   const long long grid_target = static_cast<long long>(ds.sms) * ctas_per_sm;
   const long long rpc = std::max<long long>(1, (rows + grid_target - 1) / grid_target);
+  p.a.in_dim = static_cast<int>(in_dim);
   p.a.rows = static_cast<int>(rows);
   p.a.RB = static_cast<int>(RB);
   p.a.U = static_cast<int>(U);
   p.a.TS = TS;
   p.a.RPI = RPI;
   p.a.rows_per_cta = static_cast<int>(rpc);
-  p.threads = threads;
+  p.threads = 32 + TS * RPI;
   p.grid = static_cast<int>((rows + rpc - 1) / rpc);
   p.upt = upt;
+  return true;
+}
+
+struct MmaPlan {
+  m3g::MmaArgs a;
+  int grid = 0;
+  size_t smem = 0;
+};
+
+bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t* w, const float* x,
+              const DevState& ds, MmaPlan& p) {
+  if (g_tune.force_generic || !g_tune.mma) return false;
+  if (in_dim % 256) return false;
+  const long long NSB = in_dim / 256;
+  const int sbb = m3g::mma_sb_bytes(f.fmt);
+  const long long RB = NSB * sbb;
+  if (sbb == 0 || RB % 16 || reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16) return false;
+  if (rows > (1ll << 31) - 1 || in_dim > (1 << 20)) return false;
+  long long KC = std::min<long long>(NSB, f.fmt == 8 ? 8 : 16);
+  if (f.fmt == 14) {  // 210-byte blocks: chunk sizes must stay multiples of 16 bytes
+    if (NSB % 8) return false;
+    KC = NSB >= 16 ? 16 : 8;
+  }
+  const long long seg = KC * sbb;
+  long long RS = (seg + 15) / 16 * 16;
+  while (RS % 128 != 32) RS += 16;
+  const long long xsl = 3 * in_dim, s32 = in_dim / 8, s16 = in_dim / 4, sc = NSB * 4;
+  const long long fixed = xsl + s32 + s16 + sc + 4 * 128 + 16;
+  const long long budget = ds.smem_optin;
+  const long long per_stage = 16 * RS + 16 * 8 * 4 + 16;
+  long long NS = std::min<long long>(g_tune.mma_stages, (budget - fixed) / per_stage);
+  if (NS < 2) return false;
+  long long off = NS * 16 * RS;
+  p.a.off_xsl = static_cast<int>(off);
+  off += (xsl + 127) / 128 * 128;
+  p.a.off_sum32 = static_cast<int>(off);
+  off += (s32 + 15) / 16 * 16;
+  p.a.off_sum16 = static_cast<int>(off);
+  off += (s16 + 15) / 16 * 16;
+  p.a.off_scale = static_cast<int>(off);
+  off += (sc + 15) / 16 * 16;
+  p.a.off_red = static_cast<int>(off);
+  off += NS * 16 * 8 * 4;
+  p.a.off_bar = static_cast<int>(off);
+  off += NS * 16 + 16;
+  if (off > budget) return false;
+  p.smem = static_cast<size_t>(off);
+  p.a.rows = static_cast<int>(rows);
+  p.a.RB = static_cast<int>(RB);
+  p.a.NSB = static_cast<int>(NSB);
+  p.a.KC = static_cast<int>(KC);
+  p.a.NKC = static_cast<int>((NSB + KC - 1) / KC);
+  p.a.RS = static_cast<int>(RS);
+  p.a.NS = static_cast<int>(NS);
+  const long long rpc = std::max<long long>(1, (rows + ds.sms - 1) / ds.sms);
+  p.a.rows_per_cta = static_cast<int>(rpc);
+  p.grid = static_cast<int>((rows + rpc - 1) / rpc);
   return true;
 }
 
 // y[out_dim] = W x on `st`; w/x/y device pointers.
 int gemv_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const float* x, float* y,
                 long long in_dim, long long out_dim, cudaStream_t st) {
+  MmaPlan mp;
+  if (plan_mma(f, in_dim, out_dim, w, x, ds, mp)) {
+    mp.a.w = w;
+    mp.a.x = x;
+    mp.a.y = y;
+    mp.a.status = ds.status;
+    cudaError_t e = m3g::launch_gemv_mma(f.fmt, mp.a, mp.grid, mp.smem, st, g_tune.pdl != 0);
+    if (e != cudaSuccess) return cuda_fail(e, "k_gemv_mma launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return M3G_OK;
+  }
   StreamPlan p;
-  if (plan_stream(f, in_dim, out_dim, w, ds, p)) {
+  if (plan_stream(f, in_dim, out_dim, w, x, ds, p)) {
     p.a.w = w;
     p.a.x = x;
     p.a.y = y;
     p.a.status = ds.status;
-    cudaError_t e = m3g::launch_gemv_stream(f.fmt, p.a, p.threads, p.grid, p.smem, p.upt, st);
+    cudaError_t e = m3g::launch_gemv_stream(f.fmt, p.a, p.threads, p.grid, p.smem, p.upt, st, g_tune.pdl != 0);
     if (e != cudaSuccess) return cuda_fail(e, "k_gemv_stream launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return M3G_OK;
@@ -266,6 +350,9 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "ctas_per_sm") && value >= 1 && value <= 8) g_tune.ctas_per_sm = value;
   else if (!strcmp(key, "max_stages") && value >= 2 && value <= 32) g_tune.max_stages = value;
   else if (!strcmp(key, "force_generic")) g_tune.force_generic = value != 0;
+  else if (!strcmp(key, "pdl")) g_tune.pdl = value != 0;
+  else if (!strcmp(key, "mma")) g_tune.mma = value != 0;
+  else if (!strcmp(key, "mma_stages") && value >= 2 && value <= 8) g_tune.mma_stages = value;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }
@@ -405,7 +492,6 @@ int m3g_dequantize_dev(const uint8_t* src, uint64_t src_len, uint32_t dtype, flo
                        void* stream) {
   if ((!src && src_len) || (!dst && n)) return fail(M3G_EINVAL, "null pointer");
   int fmt = -1;
-  uint64_t need = 0;
   switch (dtype) {
     case 0: if (src_len < n * 4) return fail(M3G_ENONE, "F32 source too short"); fmt = 0; break;
     case 1: if (src_len < n * 2) return fail(M3G_ENONE, "F16 source too short"); fmt = 1; break;
@@ -428,7 +514,6 @@ int m3g_dequantize_dev(const uint8_t* src, uint64_t src_len, uint32_t dtype, flo
     default:
       return fail(M3G_ENONE, "dequantize: unsupported dtype %u", dtype);
   }
-  (void)need;
   if (n == 0) return M3G_OK;
   DevState* ds = nullptr;
   if (int rc = current_dev_state(&ds)) return rc;

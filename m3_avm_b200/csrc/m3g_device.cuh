@@ -108,15 +108,35 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Wait for phase `parity` of `bar` to complete, giving up after ~timeout_ns
-// of wall time or 2^26 polls, whichever comes first.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+// of wall time or 2^26 polls, whichever comes first, or as soon as another
+// thread of the CTA has raised *abort (checked every 256 polls).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
+                                                  const volatile int* abort = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1; it < (1u << 26); ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u && global_ns() - t0 > timeout_ns) return false;
+    if ((it & 255u) == 0u) {
+      if (abort && *abort) return false;
+      if (global_ns() - t0 > timeout_ns) return false;
+    }
   }
   return false;
 }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Named barrier over the first `count` threads' warps that execute it (id 1..15).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Programmatic dependent launch: block until the grids this launch depends on
+// have completed and flushed memory (no-op for an ordinary launch), and allow
+// the next dependent grid to begin its pre-wait prologue.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace m3g

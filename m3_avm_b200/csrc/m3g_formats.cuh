@@ -66,20 +66,21 @@ struct FmtQ4K {
     uint32_t sc_a, m_a, sc_b, m_b;
     scales(hdr.y, hdr.z, hdr.w, c, sc_a, m_a, sc_b, m_b);
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    float lo = 0.f, hi = 0.f;
+    float lo0 = 0.f, lo1 = 0.f, hi0 = 0.f, hi1 = 0.f;  // four short FMA chains
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       const uint32_t l = q[w] & 0x0F0F0F0Fu;
       const uint32_t h = (q[w] >> 4) & 0x0F0F0F0Fu;
-      lo = fmaf(byte_2p23<0>(l) - k2p23, x[4 * w + 0], lo);
-      lo = fmaf(byte_2p23<1>(l) - k2p23, x[4 * w + 1], lo);
-      lo = fmaf(byte_2p23<2>(l) - k2p23, x[4 * w + 2], lo);
-      lo = fmaf(byte_2p23<3>(l) - k2p23, x[4 * w + 3], lo);
-      hi = fmaf(byte_2p23<0>(h) - k2p23, x[32 + 4 * w + 0], hi);
-      hi = fmaf(byte_2p23<1>(h) - k2p23, x[32 + 4 * w + 1], hi);
-      hi = fmaf(byte_2p23<2>(h) - k2p23, x[32 + 4 * w + 2], hi);
-      hi = fmaf(byte_2p23<3>(h) - k2p23, x[32 + 4 * w + 3], hi);
+      lo0 = fmaf(byte_2p23<0>(l) - k2p23, x[4 * w + 0], lo0);
+      lo1 = fmaf(byte_2p23<1>(l) - k2p23, x[4 * w + 1], lo1);
+      lo0 = fmaf(byte_2p23<2>(l) - k2p23, x[4 * w + 2], lo0);
+      lo1 = fmaf(byte_2p23<3>(l) - k2p23, x[4 * w + 3], lo1);
+      hi0 = fmaf(byte_2p23<0>(h) - k2p23, x[32 + 4 * w + 0], hi0);
+      hi1 = fmaf(byte_2p23<1>(h) - k2p23, x[32 + 4 * w + 1], hi1);
+      hi0 = fmaf(byte_2p23<2>(h) - k2p23, x[32 + 4 * w + 2], hi0);
+      hi1 = fmaf(byte_2p23<3>(h) - k2p23, x[32 + 4 * w + 3], hi1);
     }
+    const float lo = lo0 + lo1, hi = hi0 + hi1;
     const float d1 = d * (float)sc_a, d2 = d * (float)sc_b;
     const float m1 = dmin * (float)m_a, m2 = dmin * (float)m_b;
     return (d1 * lo - m1 * e[0]) + (d2 * hi - m2 * e[1]);
@@ -151,16 +152,16 @@ struct FmtQ80 {
     lds_words<8>(blk + 2, Q);
     const float d = f16_to_f32(*reinterpret_cast<const uint16_t*>(blk));
     constexpr float kBias = 8388608.0f + 128.0f;  // int8 q stored as (q ^ 0x80) = q + 128
-    float s = 0.f;
+    float s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       const uint32_t v = Q[w] ^ 0x80808080u;
-      s = fmaf(byte_2p23<0>(v) - kBias, x[4 * w + 0], s);
-      s = fmaf(byte_2p23<1>(v) - kBias, x[4 * w + 1], s);
-      s = fmaf(byte_2p23<2>(v) - kBias, x[4 * w + 2], s);
-      s = fmaf(byte_2p23<3>(v) - kBias, x[4 * w + 3], s);
+      s0 = fmaf(byte_2p23<0>(v) - kBias, x[4 * w + 0], s0);
+      s1 = fmaf(byte_2p23<1>(v) - kBias, x[4 * w + 1], s1);
+      s0 = fmaf(byte_2p23<2>(v) - kBias, x[4 * w + 2], s0);
+      s1 = fmaf(byte_2p23<3>(v) - kBias, x[4 * w + 3], s1);
     }
-    return d * s;
+    return d * (s0 + s1);
   }
 };
 
@@ -180,20 +181,20 @@ struct FmtQ40 {
     lds_words<4>(blk + 2, Q);
     const float d = f16_to_f32(*reinterpret_cast<const uint16_t*>(blk));
     constexpr float kBias = 8388608.0f + 8.0f;
-    float s = 0.f;
+    float s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const uint32_t l = Q[w] & 0x0F0F0F0Fu, h = (Q[w] >> 4) & 0x0F0F0F0Fu;
-      s = fmaf(byte_2p23<0>(l) - kBias, x[4 * w + 0], s);
-      s = fmaf(byte_2p23<1>(l) - kBias, x[4 * w + 1], s);
-      s = fmaf(byte_2p23<2>(l) - kBias, x[4 * w + 2], s);
-      s = fmaf(byte_2p23<3>(l) - kBias, x[4 * w + 3], s);
-      s = fmaf(byte_2p23<0>(h) - kBias, x[16 + 4 * w + 0], s);
-      s = fmaf(byte_2p23<1>(h) - kBias, x[16 + 4 * w + 1], s);
-      s = fmaf(byte_2p23<2>(h) - kBias, x[16 + 4 * w + 2], s);
-      s = fmaf(byte_2p23<3>(h) - kBias, x[16 + 4 * w + 3], s);
+      s0 = fmaf(byte_2p23<0>(l) - kBias, x[4 * w + 0], s0);
+      s1 = fmaf(byte_2p23<1>(l) - kBias, x[4 * w + 1], s1);
+      s0 = fmaf(byte_2p23<2>(l) - kBias, x[4 * w + 2], s0);
+      s1 = fmaf(byte_2p23<3>(l) - kBias, x[4 * w + 3], s1);
+      s0 = fmaf(byte_2p23<0>(h) - kBias, x[16 + 4 * w + 0], s0);
+      s1 = fmaf(byte_2p23<1>(h) - kBias, x[16 + 4 * w + 1], s1);
+      s0 = fmaf(byte_2p23<2>(h) - kBias, x[16 + 4 * w + 2], s0);
+      s1 = fmaf(byte_2p23<3>(h) - kBias, x[16 + 4 * w + 3], s1);
     }
-    return d * s;
+    return d * (s0 + s1);
   }
 };
 

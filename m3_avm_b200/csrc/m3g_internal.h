@@ -11,24 +11,54 @@ enum : uint32_t {
 };
 
 // Arguments of the staged streaming GEMV (k_gemv_stream).
+// Block = one producer warp + TS*RPI consumer threads.  Shared memory:
+//   [0, NS*stage_stride)          weight stages (TMA bulk destinations)
+//   [off_x, off_x + 4*in_dim)     x staged by the consumers (when stage_x)
+//   [off_red, ...)                per-stage row partials [NS][R][TS/32]
+//   [off_bar, ...)                full[NS], empty[NS] mbarriers, abort flag
 struct StreamArgs {
   const uint8_t* w;   // weight bytes of rows [0, rows), row-major, RB bytes per row, 16-byte aligned
   const float* x;     // x[in_dim]
   float* y;           // y[rows]
   uint32_t* status;   // per-device error word
+  int in_dim;         // K
   int rows;           // output rows handled by this launch
   int RB;             // bytes per row (multiple of 16)
   int U;              // units per row = in_dim / unit elements
-  int TS;             // threads per row slot (multiple of 32, >= ceil(U / UPT))
-  int RPI;            // row slots per CTA (blockDim = TS * RPI)
-  int R;              // rows per stage (multiple of RPI, <= TS)
+  int TS;             // consumer threads per row slot (multiple of 32, >= ceil(U / UPT))
+  int RPI;            // row slots per CTA
+  int R;              // rows per stage (multiple of RPI)
   int NS;             // pipeline stages
   int stage_stride;   // bytes between stage buffers (>= R*RB + 16, multiple of 128)
   int rows_per_cta;   // contiguous rows per CTA
+  int stage_x;        // 1: consumers stage x in shared memory with coalesced loads
+  int off_x, off_red, off_bar;
 };
 
+// Arguments of the tensor-core GEMV (k_gemv_mma).  Block = one producer warp
+// + 8 consumer warps.  Stage s holds k-chunk (s % NKC) of 16-row tile
+// (s / NKC): 16 row segments of up to KC super-blocks, RS bytes apart.
+struct MmaArgs {
+  const uint8_t* w;   // weight bytes, RB per row, 16-byte aligned
+  const float* x;     // x[in_dim], 16-byte aligned
+  float* y;           // y[rows]
+  uint32_t* status;   // per-device error word
+  int rows;
+  int RB;             // bytes per row
+  int NSB;            // super-blocks per row (in_dim / 256)
+  int KC;             // super-blocks per k-chunk
+  int NKC;            // k-chunks per tile
+  int RS;             // shared-memory stride of a staged row segment
+  int NS;             // stages
+  int rows_per_cta;
+  int off_xsl, off_sum32, off_sum16, off_scale, off_red, off_bar;
+};
+
+int mma_sb_bytes(int fmt);
+cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int grid, size_t smem, cudaStream_t st, bool pdl);
+
 cudaError_t launch_gemv_stream(int fmt, const StreamArgs& a, int threads, int grid, size_t smem, int upt,
-                               cudaStream_t st);
+                               cudaStream_t st, bool pdl);
 cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float* y, long long in_dim,
                                 long long nblocks, int grid, cudaStream_t st);
 cudaError_t launch_dequant(int fmt, const uint8_t* w, float* out, long long n_elems, int grid, cudaStream_t st);

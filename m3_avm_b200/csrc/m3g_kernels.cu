@@ -10,6 +10,7 @@
 //                         output rows (in_dim not a multiple of the block):
 //                         one warp per block, exact decode, atomics per row.
 // k_dequant<...>          bit-exact block decode to f32 (src/quant.rs:9-173).
+#include <atomic>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -24,26 +25,103 @@ namespace m3g {
 constexpr uint64_t kCopyTimeoutNs = 2000000000ull;
 
 template <class F, int UPT>
-__global__ void __launch_bounds__(256) k_gemv_stream(const StreamArgs a) {
+__global__ void __launch_bounds__(288) k_gemv_stream(const StreamArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x;
-  const int slot = tid / a.TS;
-  const int ls = tid - slot * a.TS;
-  const int lane = tid & 31;
-  const int wis = ls >> 5;
-  const int WPS = a.TS >> 5;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int WPS = a.TS >> 5;               // consumer warps per row slot
+  const int NC = a.TS * a.RPI;             // consumer threads
+  const int NCW = NC >> 5;                 // consumer warps
 
   const long long row0 = static_cast<long long>(blockIdx.x) * a.rows_per_cta;
   long long row_end = row0 + a.rows_per_cta;
   if (row_end > a.rows) row_end = a.rows;
-  if (row0 >= row_end) return;
+  if (row0 >= row_end) return;             // uniform across the CTA
   const int nrows = static_cast<int>(row_end - row0);
   const int nst = (nrows + a.R - 1) / a.R;
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(a.NS) * a.stage_stride);
-  float* red = reinterpret_cast<float*>(bars + a.NS);
+  float* xs = reinterpret_cast<float*>(smem + a.off_x);
+  float* red = reinterpret_cast<float*>(smem + a.off_red);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+  uint64_t* empty = full + a.NS;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + a.NS);
+  const uint8_t* wbase = a.w + row0 * static_cast<long long>(a.RB);
 
-  // x of this thread's units, resident in registers for the whole kernel.
+  if (tid == 0) {
+    for (int s = 0; s < a.NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], static_cast<uint32_t>(NCW));
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------ producer warp
+    uint64_t policy = 0;
+    int issued = 0;
+    auto issue = [&](int s) {
+      const int rows_s = min(a.R, nrows - s * a.R);
+      const uint32_t bytes = static_cast<uint32_t>(rows_s) * static_cast<uint32_t>(a.RB);
+      const int b = s % a.NS;
+      mbar_arrive_expect_tx(&full[b], bytes);
+      bulk_g2s(smem + static_cast<size_t>(b) * a.stage_stride, wbase + static_cast<long long>(s) * a.R * a.RB,
+               bytes, &full[b], policy);
+    };
+    if (lane == 0) {
+      // Weights are never written by an earlier kernel, so their stream starts
+      // before the grid dependency resolves.
+      policy = l2_evict_first_policy();
+      const int pre = min(a.NS, nst);
+      for (int s = 0; s < pre; ++s) issue(s);
+      issued = pre;
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+    int buf = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int s = 0; s < nst; ++s) {
+      ok = mbar_wait_bounded(&empty[buf], ph, kCopyTimeoutNs, abort_flag);
+      if (!ok) break;
+      const int rows_s = min(a.R, nrows - s * a.R);
+      const float* rb = red + static_cast<size_t>(buf) * a.R * WPS;
+      for (int r = lane; r < rows_s; r += 32) {
+        float acc = 0.f;
+        for (int w = 0; w < WPS; ++w) acc += rb[r * WPS + w];
+        a.y[row0 + static_cast<long long>(s) * a.R + r] = acc;
+      }
+      __syncwarp();
+      if (lane == 0 && s + a.NS < nst) {
+        fence_proxy_async_smem();
+        issue(s + a.NS);
+        issued = s + a.NS + 1;
+      }
+      if (++buf == a.NS) { buf = 0; ph ^= 1u; }
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      atomicOr(a.status, kStatusCopyTimeout);
+      // Let copies still in flight land (bounded) before the CTA exits.
+      for (int s = max(0, issued - a.NS); s < issued; ++s)
+        (void)mbar_wait_bounded(&full[s % a.NS], static_cast<uint32_t>(s / a.NS) & 1u, kCopyTimeoutNs);
+    }
+    return;
+  }
+
+  // -------------------------------------------------- consumer warps
+  const int ctid = tid - 32;
+  const int slot = ctid / a.TS;
+  const int ls = ctid - slot * a.TS;
+  const int wis = ls >> 5;
+  grid_dep_wait();
+  if (a.stage_x) {
+    const float4* xg = reinterpret_cast<const float4*>(a.x);
+    float4* xs4 = reinterpret_cast<float4*>(xs);
+    for (int i = ctid; i < (a.in_dim >> 2); i += NC) xs4[i] = __ldg(xg + i);
+    named_bar_sync(1, NC);
+  }
   float xr[UPT][F::kUnitElems];
   float xe[UPT][F::kExtra];
   bool act[UPT];
@@ -51,70 +129,50 @@ __global__ void __launch_bounds__(256) k_gemv_stream(const StreamArgs a) {
   for (int k = 0; k < UPT; ++k) {
     const int u = ls + k * a.TS;
     act[k] = u < a.U;
+    if (a.stage_x) {
 #pragma unroll
-    for (int i = 0; i < F::kUnitElems; ++i) xr[k][i] = act[k] ? __ldg(a.x + F::xpos(u, i)) : 0.f;
+      for (int i = 0; i < F::kUnitElems; i += 4) {
+        const float4 v = act[k] ? *reinterpret_cast<const float4*>(xs + F::xpos(u, i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xr[k][i] = v.x; xr[k][i + 1] = v.y; xr[k][i + 2] = v.z; xr[k][i + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < F::kUnitElems; i += 4) {
+        const float4 v = act[k] ? __ldg(reinterpret_cast<const float4*>(a.x + F::xpos(u, i))) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xr[k][i] = v.x; xr[k][i + 1] = v.y; xr[k][i + 2] = v.z; xr[k][i + 3] = v.w;
+      }
+    }
     F::prep(xr[k], xe[k]);
   }
 
-  const uint8_t* wbase = a.w + row0 * static_cast<long long>(a.RB);
-  uint64_t policy = 0;
-  if (tid == 0) {
-    for (int s = 0; s < a.NS; ++s) mbar_init(&bars[s], 1);
-    fence_mbar_init();
-    policy = l2_evict_first_policy();
-  }
-  __syncthreads();
-
-  auto issue = [&](int s) {
-    const int rows_s = min(a.R, nrows - s * a.R);
-    const uint32_t bytes = static_cast<uint32_t>(rows_s) * static_cast<uint32_t>(a.RB);
-    uint64_t* bar = &bars[s % a.NS];
-    mbar_arrive_expect_tx(bar, bytes);
-    bulk_g2s(smem + static_cast<size_t>(s % a.NS) * a.stage_stride,
-             wbase + static_cast<long long>(s) * a.R * a.RB, bytes, bar, policy);
-  };
-  if (tid == 0) {
-    const int pre = min(a.NS, nst);
-    for (int s = 0; s < pre; ++s) issue(s);
-  }
-
+  int buf = 0;
+  uint32_t ph = 0;
   for (int i = 0; i < nst; ++i) {
-    const int buf = i % a.NS;
-    const uint32_t par = static_cast<uint32_t>(i / a.NS) & 1u;
-    const bool ok = mbar_wait_bounded(&bars[buf], par, kCopyTimeoutNs);
+    const bool ok = mbar_wait_bounded(&full[buf], ph, kCopyTimeoutNs, abort_flag);
+    if (!ok) {
+      if (lane == 0) {
+        *abort_flag = 1;
+        atomicOr(a.status, kStatusCopyTimeout);
+      }
+      return;
+    }
     const uint8_t* sb = smem + static_cast<size_t>(buf) * a.stage_stride;
     const int rows_here = min(a.R, nrows - i * a.R);
-    float* redb = red + (i & 1) * a.R * WPS;
+    float* rb = red + static_cast<size_t>(buf) * a.R * WPS;
     for (int rr = slot; rr < a.R; rr += a.RPI) {
       float acc = 0.f;
-      if (ok && rr < rows_here) {
+      if (rr < rows_here) {
         const uint8_t* rowp = sb + static_cast<size_t>(rr) * a.RB;
 #pragma unroll
         for (int k = 0; k < UPT; ++k)
           if (act[k]) acc += F::dot(rowp, ls + k * a.TS, xr[k], xe[k]);
       }
       acc = warp_sum(acc);
-      if (lane == 0) redb[rr * WPS + wis] = acc;
+      if (lane == 0) rb[rr * WPS + wis] = acc;
     }
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0) {
-        atomicOr(a.status, kStatusCopyTimeout);
-        // Let the copies still in flight land (bounded) before the CTA exits.
-        const int last = min(nst, i + a.NS);
-        for (int s = i; s < last; ++s)
-          (void)mbar_wait_bounded(&bars[s % a.NS], static_cast<uint32_t>(s / a.NS) & 1u, kCopyTimeoutNs);
-      }
-      return;
-    }
-    if (tid == 0 && i + a.NS < nst) {
-      fence_proxy_async_smem();
-      issue(i + a.NS);
-    }
-    if (tid < rows_here) {
-      float s = 0.f;
-      for (int w = 0; w < WPS; ++w) s += redb[tid * WPS + w];
-      a.y[row0 + static_cast<long long>(i) * a.R + tid] = s;
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[buf]);
+    if (++buf == a.NS) { buf = 0; ph ^= 1u; }
   }
 }
 
@@ -197,33 +255,60 @@ __global__ void k_dequant_f16(const uint8_t* __restrict__ w, float* __restrict__
 
 // ---------------------------------------------------------------- launchers
 
+// Raise a kernel's dynamic shared-memory limit once per device to the
+// largest size requested so far (the attribute is per device context).
+template <auto Kern>
+static cudaError_t ensure_smem(size_t smem) {
+  constexpr int kMaxDev = 64;
+  static std::atomic<int> limit[kMaxDev];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  if (static_cast<int>(smem) <= limit[dev].load(std::memory_order_relaxed)) return cudaSuccess;
+  e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess) {
+    int cur = limit[dev].load();
+    while (cur < static_cast<int>(smem) && !limit[dev].compare_exchange_weak(cur, static_cast<int>(smem))) {
+    }
+  }
+  return e;
+}
+
+template <auto Kern>
+static cudaError_t launch_pdl(const StreamArgs& a, int threads, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  cudaError_t e = ensure_smem<Kern>(smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, Kern, a);
+}
+
 template <class F>
 static cudaError_t launch_stream_fmt(const StreamArgs& a, int threads, int grid, size_t smem, int upt,
-                                     cudaStream_t st) {
-  cudaError_t e = cudaSuccess;
+                                     cudaStream_t st, bool pdl) {
   switch (upt) {
-    case 1:
-      e = cudaFuncSetAttribute(k_gemv_stream<F, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) k_gemv_stream<F, 1><<<grid, threads, smem, st>>>(a);
-      break;
-    case 2:
-      e = cudaFuncSetAttribute(k_gemv_stream<F, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) k_gemv_stream<F, 2><<<grid, threads, smem, st>>>(a);
-      break;
-    default:
-      return cudaErrorInvalidValue;
+    case 1: return launch_pdl<k_gemv_stream<F, 1>>(a, threads, grid, smem, st, pdl);
+    case 2: return launch_pdl<k_gemv_stream<F, 2>>(a, threads, grid, smem, st, pdl);
+    default: return cudaErrorInvalidValue;
   }
-  if (e != cudaSuccess) return e;
-  return cudaGetLastError();
 }
 
 cudaError_t launch_gemv_stream(int fmt, const StreamArgs& a, int threads, int grid, size_t smem, int upt,
-                               cudaStream_t st) {
+                               cudaStream_t st, bool pdl) {
   switch (fmt) {
-    case 12: return launch_stream_fmt<FmtQ4K>(a, threads, grid, smem, upt, st);
-    case 14: return launch_stream_fmt<FmtQ6K>(a, threads, grid, smem, upt, st);
-    case 8: return launch_stream_fmt<FmtQ80>(a, threads, grid, smem, upt, st);
-    case 2: return launch_stream_fmt<FmtQ40>(a, threads, grid, smem, upt, st);
+    case 12: return launch_stream_fmt<FmtQ4K>(a, threads, grid, smem, upt, st, pdl);
+    case 14: return launch_stream_fmt<FmtQ6K>(a, threads, grid, smem, upt, st, pdl);
+    case 8: return launch_stream_fmt<FmtQ80>(a, threads, grid, smem, upt, st, pdl);
+    case 2: return launch_stream_fmt<FmtQ40>(a, threads, grid, smem, upt, st, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -140,9 +140,26 @@ SHAPES = [
 ]
 
 
+KERNELS = {
+    # tuning that selects each kernel where the shape allows it
+    "mma": {},
+    "stream": {"mma": 0},
+    "generic": {"force_generic": 1},
+}
+
+
+@pytest.fixture(params=list(KERNELS))
+def kernel(request, m3):
+    for k, v in KERNELS[request.param].items():
+        m3.matvec_quant.set_tuning(k, v)
+    yield request.param
+    m3.matvec_quant.set_tuning("mma", 1)
+    m3.matvec_quant.set_tuning("force_generic", 0)
+
+
 @pytest.mark.parametrize("dtype", [2, 8, 12, 14])
 @pytest.mark.parametrize("shape", SHAPES)
-def test_gemv_matches_oracle(m3, dtype, shape):
+def test_gemv_matches_oracle(m3, kernel, dtype, shape):
     in_dim, out_dim = shape
     be, _ = BLOCK[dtype]
     if (in_dim * out_dim) % be:
@@ -250,7 +267,9 @@ def test_gemv_batched_dev_matches_oracle(m3):
     (12, 4096, 14336),    # FFN gate/up
     (14, 14336, 4096),    # FFN down
     (8, 4096, 4096),      # Q8_0
+    (2, 4096, 4096),      # Q4_0
     (14, 4096, 128256),   # vocab head
+    (12, 8192, 28672),    # batched-decode weight, one column
 ])
 def test_benchmark_shapes_match_oracle(m3, dtype, in_dim, out_dim):
     import torch
