@@ -79,7 +79,14 @@ struct Tuning {
   int64_t force_generic = 0;    // route every GEMV through the generic kernel (parity tests)
   int64_t pdl = 1;              // programmatic dependent launch of the streaming kernels
   int64_t mma = 1;              // tensor-core GEMV where the shape allows it
-  int64_t mma_stages = 4;       // pipeline stages of the tensor-core GEMV
+  int64_t mma_stages = 5;       // pipeline stages of the tensor-core GEMV
+  int64_t mma_tps = 1;          // 16-row tiles per stage (1: 8 consumer warps, 2: 16)
+  int64_t mma_kc = 16;          // super-blocks per k-chunk (<= 16)
+  int64_t mma_ctas = 1;         // CTAs per SM the tensor-core GEMV is sized for
+  int64_t mma_wk = 0;           // consumer warps splitting a tile's k-chunk (8, 16; 0 = by shape)
+  int64_t mma_cg = 4;           // rows per bulk copy when rows are contiguous (1 or 4)
+  int64_t mma_pre = 1;          // stages prefetched before the previous kernel finishes
+  int64_t mma_coresident = 0;   // size CTAs for half an SM so consecutive GEMVs overlap
 };
 Tuning g_tune;
 
@@ -199,7 +206,7 @@ bool plan_stream(const FmtInfo& f, long long in_dim, long long rows, const uint8
 
 struct MmaPlan {
   m3g::MmaArgs a;
-  int grid = 0;
+  int grid = 0, tps = 1, wk = 8;
   size_t smem = 0;
 };
 
@@ -212,21 +219,37 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   const long long RB = NSB * sbb;
   if (sbb == 0 || RB % 16 || reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16) return false;
   if (rows > (1ll << 31) - 1 || in_dim > (1 << 20)) return false;
-  long long KC = std::min<long long>(NSB, f.fmt == 8 ? 8 : 16);
+  long long KC = std::min<long long>(NSB, std::min<int64_t>(16, g_tune.mma_kc));
+  // Consumer warps per tile: 16 when a k-chunk of 16 super-blocks covers the
+  // whole row (one super-block per warp, x operands stay in registers), or
+  // for the heavier Q6_K decode; 8 otherwise.  mma_wk = 8 / 16 forces it.
+  int wk = g_tune.mma_wk;
+  if (wk != 8 && wk != 16) wk = ((NSB == 16 && KC == 16) || (f.fmt == 14 && NSB >= 16)) ? 16 : 8;
+  const int tps = wk == 16 ? 1 : static_cast<int>(std::min<int64_t>(2, std::max<int64_t>(1, g_tune.mma_tps)));
   if (f.fmt == 14) {  // 210-byte blocks: chunk sizes must stay multiples of 16 bytes
     if (NSB % 8) return false;
-    KC = NSB >= 16 ? 16 : 8;
+    KC = std::max<long long>(8, KC / 8 * 8);
+    if (KC > NSB) KC = NSB;
   }
   const long long seg = KC * sbb;
-  long long RS = (seg + 15) / 16 * 16;
-  while (RS % 128 != 32) RS += 16;
+  const long long NKC = (NSB + KC - 1) / KC;
+  // Whole rows are contiguous when one k-chunk covers the row: copy 4 rows
+  // per bulk copy then; otherwise one copy per row segment.
+  const long long CG = (NKC == 1 && g_tune.mma_cg == 4) ? 4 : 1;
+  long long GS = (CG * seg + 15) / 16 * 16;
+  while (GS % 128 != 32) GS += 16;
   const long long xsl = 3 * in_dim, s32 = in_dim / 8, s16 = in_dim / 4, sc = NSB * 4;
   const long long fixed = xsl + s32 + s16 + sc + 4 * 128 + 16;
-  const long long budget = ds.smem_optin;
-  const long long per_stage = 16 * RS + 16 * 8 * 4 + 16;
+  const long long mctas = std::max<int64_t>(1, g_tune.mma_ctas);
+  // mma_coresident sizes a CTA for half an SM without changing the grid, so
+  // the next GEMV's CTAs (launched early by PDL) fit beside this one's.
+  const long long div = std::max<long long>(mctas, g_tune.mma_coresident ? 2 : 1);
+  const long long budget = std::min<long long>(ds.smem_optin, ds.smem_per_sm / div - 1024);
+  const long long SR = 16 * tps;
+  const long long per_stage = SR / CG * GS + SR * wk * 4 + 16;
   long long NS = std::min<long long>(g_tune.mma_stages, (budget - fixed) / per_stage);
   if (NS < 2) return false;
-  long long off = NS * 16 * RS;
+  long long off = NS * (SR / CG) * GS;
   p.a.off_xsl = static_cast<int>(off);
   off += (xsl + 127) / 128 * 128;
   p.a.off_sum32 = static_cast<int>(off);
@@ -236,7 +259,7 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   p.a.off_scale = static_cast<int>(off);
   off += (sc + 15) / 16 * 16;
   p.a.off_red = static_cast<int>(off);
-  off += NS * 16 * 8 * 4;
+  off += NS * SR * wk * 4;
   p.a.off_bar = static_cast<int>(off);
   off += NS * 16 + 16;
   if (off > budget) return false;
@@ -245,10 +268,16 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   p.a.RB = static_cast<int>(RB);
   p.a.NSB = static_cast<int>(NSB);
   p.a.KC = static_cast<int>(KC);
-  p.a.NKC = static_cast<int>((NSB + KC - 1) / KC);
-  p.a.RS = static_cast<int>(RS);
+  p.a.NKC = static_cast<int>(NKC);
+  p.a.CG = static_cast<int>(CG);
+  p.a.GS = static_cast<int>(GS);
+  p.a.SEG = static_cast<int>(seg);
   p.a.NS = static_cast<int>(NS);
-  const long long rpc = std::max<long long>(1, (rows + ds.sms - 1) / ds.sms);
+  p.a.PRE = static_cast<int>(std::max<int64_t>(0, g_tune.mma_pre));
+  p.tps = tps;
+  p.wk = wk;
+  const long long ctas = static_cast<long long>(ds.sms) * mctas;
+  const long long rpc = std::max<long long>(1, (rows + ctas - 1) / ctas);
   p.a.rows_per_cta = static_cast<int>(rpc);
   p.grid = static_cast<int>((rows + rpc - 1) / rpc);
   return true;
@@ -263,7 +292,7 @@ int gemv_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const fl
     mp.a.x = x;
     mp.a.y = y;
     mp.a.status = ds.status;
-    cudaError_t e = m3g::launch_gemv_mma(f.fmt, mp.a, mp.grid, mp.smem, st, g_tune.pdl != 0);
+    cudaError_t e = m3g::launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);
     if (e != cudaSuccess) return cuda_fail(e, "k_gemv_mma launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return M3G_OK;
@@ -353,6 +382,13 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "pdl")) g_tune.pdl = value != 0;
   else if (!strcmp(key, "mma")) g_tune.mma = value != 0;
   else if (!strcmp(key, "mma_stages") && value >= 2 && value <= 8) g_tune.mma_stages = value;
+  else if (!strcmp(key, "mma_tps") && value >= 1 && value <= 2) g_tune.mma_tps = value;
+  else if (!strcmp(key, "mma_kc") && value >= 1 && value <= 16) g_tune.mma_kc = value;
+  else if (!strcmp(key, "mma_ctas") && value >= 1 && value <= 2) g_tune.mma_ctas = value;
+  else if (!strcmp(key, "mma_wk") && (value == 0 || value == 8 || value == 16)) g_tune.mma_wk = value;
+  else if (!strcmp(key, "mma_cg") && (value == 1 || value == 4)) g_tune.mma_cg = value;
+  else if (!strcmp(key, "mma_pre") && value >= 0 && value <= 8) g_tune.mma_pre = value;
+  else if (!strcmp(key, "mma_coresident")) g_tune.mma_coresident = value != 0;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }

@@ -36,8 +36,9 @@ struct StreamArgs {
 };
 
 // Arguments of the tensor-core GEMV (k_gemv_mma).  Block = one producer warp
-// + 8 consumer warps.  Stage s holds k-chunk (s % NKC) of 16-row tile
-// (s / NKC): 16 row segments of up to KC super-blocks, RS bytes apart.
+// + WK*TPS consumer warps.  Stage s holds k-chunk (s % NKC) of the row group
+// (s / NKC) of 16*TPS rows: each row's segment of up to KC super-blocks,
+// copied CG rows at a time into groups GS bytes apart.
 struct MmaArgs {
   const uint8_t* w;   // weight bytes, RB per row, 16-byte aligned
   const float* x;     // x[in_dim], 16-byte aligned
@@ -48,14 +49,18 @@ struct MmaArgs {
   int NSB;            // super-blocks per row (in_dim / 256)
   int KC;             // super-blocks per k-chunk
   int NKC;            // k-chunks per tile
-  int RS;             // shared-memory stride of a staged row segment
+  int CG;             // rows per bulk copy: 4 (whole rows, NKC == 1) or 1 (row segments)
+  int GS;             // shared-memory stride between copy groups (32 mod 128 bytes)
+  int SEG;            // bytes of one row's segment within a group
   int NS;             // stages
+  int PRE;            // stages issued before the grid dependency resolves
   int rows_per_cta;
   int off_xsl, off_sum32, off_sum16, off_scale, off_red, off_bar;
 };
 
 int mma_sb_bytes(int fmt);
-cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int grid, size_t smem, cudaStream_t st, bool pdl);
+cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
+                            bool pdl);
 
 cudaError_t launch_gemv_stream(int fmt, const StreamArgs& a, int threads, int grid, size_t smem, int upt,
                                cudaStream_t st, bool pdl);

@@ -28,7 +28,6 @@
 namespace m3g {
 
 constexpr uint64_t kMmaTimeoutNs = 2000000000ull;
-constexpr int kConsumerWarps = 8;
 
 __device__ __forceinline__ void mma_k32_u8s8(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                              uint32_t b1, int (&d)[4]) {
@@ -53,21 +52,24 @@ __device__ __forceinline__ void mma_k16_u8s8(uint32_t a0, uint32_t a1, uint32_t 
       : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
 
+// Shared-memory loads addressed as (dynamic shared base, 32-bit byte offset):
+// keeping offsets 32-bit lets the compiler fold them into shared addressing.
 __device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-__device__ __forceinline__ uint32_t lds16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
-
-// A 32-bit word at a 2-byte aligned shared-memory address.
-__device__ __forceinline__ uint32_t lds32_a2(const uint8_t* p) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  const uint32_t* b = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
-  return __funnelshift_r(b[0], b[1], static_cast<uint32_t>(a & 2u) * 8u);
+__device__ __forceinline__ uint2 lds64(const uint8_t* sm, uint32_t o) { return *reinterpret_cast<const uint2*>(sm + o); }
+__device__ __forceinline__ uint4 lds128(const uint8_t* sm, uint32_t o) { return *reinterpret_cast<const uint4*>(sm + o); }
+__device__ __forceinline__ uint32_t lds16(const uint8_t* sm, uint32_t o) {
+  return *reinterpret_cast<const uint16_t*>(sm + o);
 }
-// Two consecutive words at a 2-byte aligned address.
-__device__ __forceinline__ uint2 lds64_a2(const uint8_t* p) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  const uint32_t* b = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
-  const uint32_t sh = static_cast<uint32_t>(a & 2u) * 8u;
+// A 32-bit word at a 2-byte aligned offset (the base is 128-byte aligned).
+__device__ __forceinline__ uint32_t lds32_a2(const uint8_t* sm, uint32_t o) {
+  const uint32_t* b = reinterpret_cast<const uint32_t*>(sm + (o & ~3u));
+  return __funnelshift_r(b[0], b[1], (o & 2u) * 8u);
+}
+// Two consecutive words at a 2-byte aligned offset.
+__device__ __forceinline__ uint2 lds64_a2(const uint8_t* sm, uint32_t o) {
+  const uint32_t* b = reinterpret_cast<const uint32_t*>(sm + (o & ~3u));
+  const uint32_t sh = (o & 2u) * 8u;
   const uint32_t w0 = b[0], w1 = b[1], w2 = b[2];
   return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
 }
@@ -80,6 +82,19 @@ struct XPrep {
   const float* scale;  // [K/256] s_sb
 };
 
+// Zero-extended / sign-extended byte K of w (one PRMT each).  The sign form
+// uses prmt.b32 directly: __byte_perm ignores the selector's sign bit.
+template <int K>
+__device__ __forceinline__ int ubyte(uint32_t w) {
+  return static_cast<int>(__byte_perm(w, 0u, 0x4440u + K));
+}
+template <int K>
+__device__ __forceinline__ int sbyte(uint32_t w) {
+  int r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "n"((8 + K) * 0x1110 + K));
+  return r;
+}
+
 // ---------------------------------------------------------------- Q4_K
 // Super-block = one 144-byte block [d][dmin][scales 12][qs 128].  For chunk c
 // of qs, quad thread t takes qs[32c + 8t .. +8] of its two rows; with the K
@@ -89,6 +104,22 @@ struct XPrep {
 struct MmaQ4K {
   static constexpr int kSBBytes = 144;
 
+  // x operands of one super-block for this thread: B fragments of its 8
+  // sub-blocks, the sums of x over sub-blocks 2t and 2t+1, and s_sb / 16.
+  struct XB {
+    uint2 b[8];
+    float xa, xb, sx;
+  };
+
+  __device__ static __forceinline__ void load_x(const XPrep& xp, int sbg, int g, int t, XB& o) {
+    const uint8_t* xsl = xp.sl + static_cast<size_t>(sbg) * 8 * 96 + g * 32 + 8 * t;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) o.b[s] = g < 3 ? lds64(xsl + s * 96) : make_uint2(0u, 0u);
+    o.xa = xp.sum32[sbg * 8 + 2 * t];
+    o.xb = xp.sum32[sbg * 8 + 2 * t + 1];
+    o.sx = xp.scale[sbg] * (1.0f / 16.0f);
+  }
+
   __device__ static __forceinline__ void sc_words(const uint4& h, uint32_t& sc_lo, uint32_t& sc_hi, uint32_t& m_lo,
                                                   uint32_t& m_hi) {
     sc_lo = h.y & 0x3F3F3F3Fu;                                            // j < 4: q[j] & 63
@@ -97,50 +128,55 @@ struct MmaQ4K {
     m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
   }
 
-  __device__ static __forceinline__ void tile(const uint8_t* rg, const uint8_t* rg8, int sbg, const XPrep& xp, int g,
-                                              int t, float w0, float w1, float& pg, float& pg8) {
-    const uint4 hg = *reinterpret_cast<const uint4*>(rg);
-    const uint4 hg8 = *reinterpret_cast<const uint4*>(rg8);
+  __device__ static __forceinline__ void tile(const uint8_t* sm, uint32_t rg, uint32_t rg8, const XB& xb, int t,
+                                              float w0, float w1, float& pg, float& pg8) {
+    const uint4 hg = lds128(sm, rg);
+    const uint4 hg8 = lds128(sm, rg8);
+    const uint32_t qo = rg + 16 + 8 * t, qo8 = rg8 + 16 + 8 * t;
     uint32_t scl, sch, ml, mh, scl8, sch8, ml8, mh8;
     sc_words(hg, scl, sch, ml, mh);
     sc_words(hg8, scl8, sch8, ml8, mh8);
-    int acc[4] = {0, 0, 0, 0};
-    const uint8_t* xsl = xp.sl + static_cast<size_t>(sbg) * 8 * 96 + g * 32 + 8 * t;
+    int alo[4] = {0, 0, 0, 0}, ahi[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const uint2 q = lds64(rg + 16 + 32 * c + 8 * t);
-      const uint2 q8 = lds64(rg8 + 16 + 32 * c + 8 * t);
-      uint2 blo = make_uint2(0u, 0u), bhi = make_uint2(0u, 0u);
-      if (g < 3) {
-        blo = lds64(xsl + (2 * c) * 96);
-        bhi = lds64(xsl + (2 * c + 1) * 96);
-      }
+      const uint2 q = lds64(sm, qo + 32 * c);
+      const uint2 q8 = lds64(sm, qo8 + 32 * c);
       int dlo[4], dhi[4];
-      mma_k32_u8s8(q.x & 0x0F0F0F0Fu, q8.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, q8.y & 0x0F0F0F0Fu, blo.x, blo.y, dlo);
-      mma_k32_u8s8(q.x & 0xF0F0F0F0u, q8.x & 0xF0F0F0F0u, q.y & 0xF0F0F0F0u, q8.y & 0xF0F0F0F0u, bhi.x, bhi.y, dhi);
+      mma_k32_u8s8(q.x & 0x0F0F0F0Fu, q8.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, q8.y & 0x0F0F0F0Fu, xb.b[2 * c].x,
+                   xb.b[2 * c].y, dlo);
+      mma_k32_u8s8(q.x & 0xF0F0F0F0u, q8.x & 0xF0F0F0F0u, q.y & 0xF0F0F0F0u, q8.y & 0xF0F0F0F0u,
+                   xb.b[2 * c + 1].x, xb.b[2 * c + 1].y, dhi);
       const uint32_t w = c < 2 ? scl : sch, w8 = c < 2 ? scl8 : sch8;
-      const int sh = (c & 1) * 16;
-      const int sa = static_cast<int>((w >> sh) & 0xFFu) * 16, sb = static_cast<int>((w >> (sh + 8)) & 0xFFu);
-      const int sa8 = static_cast<int>((w8 >> sh) & 0xFFu) * 16, sb8 = static_cast<int>((w8 >> (sh + 8)) & 0xFFu);
-      acc[0] += sa * dlo[0] + sb * dhi[0];
-      acc[1] += sa * dlo[1] + sb * dhi[1];
-      acc[2] += sa8 * dlo[2] + sb8 * dhi[2];
-      acc[3] += sa8 * dlo[3] + sb8 * dhi[3];
+      int sa, sb, sa8, sb8;
+      if (c & 1) {
+        sa = ubyte<2>(w); sb = ubyte<3>(w); sa8 = ubyte<2>(w8); sb8 = ubyte<3>(w8);
+      } else {
+        sa = ubyte<0>(w); sb = ubyte<1>(w); sa8 = ubyte<0>(w8); sb8 = ubyte<1>(w8);
+      }
+      alo[0] += sa * dlo[0];
+      alo[1] += sa * dlo[1];
+      alo[2] += sa8 * dlo[2];
+      alo[3] += sa8 * dlo[3];
+      ahi[0] += sb * dhi[0];
+      ahi[1] += sb * dhi[1];
+      ahi[2] += sb8 * dhi[2];
+      ahi[3] += sb8 * dhi[3];
     }
-    const float sx = xp.scale[sbg] * (1.0f / 16.0f);
     const float d = f16_to_f32(hg.x), dmin = f16_to_f32(hg.x >> 16);
     const float d8 = f16_to_f32(hg8.x), dmin8 = f16_to_f32(hg8.x >> 16);
     // min term over this thread's sub-blocks j = 2t, 2t+1: dmin * sum_j m_j * sum(x_j)
     const uint32_t mw = t < 2 ? ml : mh, mw8 = t < 2 ? ml8 : mh8;
-    const int shm = (t & 1) * 16;
-    const float xa = xp.sum32[sbg * 8 + 2 * t], xb = xp.sum32[sbg * 8 + 2 * t + 1];
-    const float mg = static_cast<float>((mw >> shm) & 0xFFu) * xa + static_cast<float>((mw >> (shm + 8)) & 0xFFu) * xb;
-    const float mg8 =
-        static_cast<float>((mw8 >> shm) & 0xFFu) * xa + static_cast<float>((mw8 >> (shm + 8)) & 0xFFu) * xb;
-    const float main = static_cast<float>(acc[0]) * w0 + static_cast<float>(acc[1]) * w1;
-    const float main8 = static_cast<float>(acc[2]) * w0 + static_cast<float>(acc[3]) * w1;
-    pg += fmaf(d * sx, main, -dmin * mg);
-    pg8 += fmaf(d8 * sx, main8, -dmin8 * mg8);
+    const bool odd = t & 1;
+    const float ma = static_cast<float>(odd ? ubyte<2>(mw) : ubyte<0>(mw));
+    const float mb = static_cast<float>(odd ? ubyte<3>(mw) : ubyte<1>(mw));
+    const float ma8 = static_cast<float>(odd ? ubyte<2>(mw8) : ubyte<0>(mw8));
+    const float mb8 = static_cast<float>(odd ? ubyte<3>(mw8) : ubyte<1>(mw8));
+    const float mg = fmaf(ma, xb.xa, mb * xb.xb);
+    const float mg8 = fmaf(ma8, xb.xa, mb8 * xb.xb);
+    const float main = static_cast<float>(16 * alo[0] + ahi[0]) * w0 + static_cast<float>(16 * alo[1] + ahi[1]) * w1;
+    const float main8 = static_cast<float>(16 * alo[2] + ahi[2]) * w0 + static_cast<float>(16 * alo[3] + ahi[3]) * w1;
+    pg += fmaf(d * xb.sx, main, -dmin * mg);
+    pg8 += fmaf(d8 * xb.sx, main8, -dmin8 * mg8);
   }
 };
 
@@ -155,24 +191,52 @@ struct MmaQ4K {
 struct MmaQ6K {
   static constexpr int kSBBytes = 210;
 
-  __device__ static __forceinline__ void tile(const uint8_t* rg, const uint8_t* rg8, int sbg, const XPrep& xp, int g,
-                                              int t, float w0, float w1, float& pg, float& pg8) {
-    int acc[4] = {0, 0, 0, 0};
-    float bias = 0.f, bias8 = 0.f;
+  // B fragments of the 16 groups (index 2 * (4n + k) + h) and the x sums of
+  // the four groups whose bias this thread carries (k == t): index 2n + h.
+  struct XB {
+    uint32_t b[16];
+    float xg[4];
+    float sx;
+  };
+
+  __device__ static __forceinline__ void load_x(const XPrep& xp, int sbg, int g, int t, XB& o) {
     const uint8_t* xsl = xp.sl + static_cast<size_t>(sbg) * 8 * 96 + g * 32 + 4 * t;
 #pragma unroll
+    for (int sub = 0; sub < 8; ++sub)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) o.b[2 * sub + h] = g < 3 ? lds32(xsl + sub * 96 + 16 * h) : 0u;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) o.xg[2 * n + h] = xp.sum16[sbg * 16 + 8 * n + 2 * t + h];
+    o.sx = xp.scale[sbg];
+  }
+
+  template <int K>
+  __device__ static __forceinline__ int scale_of(const uint2& s, int h) {
+    // int8 scale 8n + h + 2K of a row: byte (h + 2K) of the two words s
+    constexpr int lo = (2 * K) & 3;
+    const uint32_t w = (2 * K) < 4 ? s.x : s.y;
+    return h ? sbyte<lo + 1>(w) : sbyte<lo>(w);
+  }
+
+  __device__ static __forceinline__ void tile(const uint8_t* sm, uint32_t rg, uint32_t rg8, const XB& xb, int t,
+                                              float w0, float w1, float& pg, float& pg8) {
+    int acc[4] = {0, 0, 0, 0};
+    float bias = 0.f, bias8 = 0.f;
+    const uint32_t qo = rg + 4 * t, qo8 = rg8 + 4 * t;
+#pragma unroll
     for (int n = 0; n < 2; ++n) {
-      // int8 scales s[8n .. 8n+8) of both rows
-      const uint2 s = lds64_a2(rg + 192 + 8 * n);
-      const uint2 s8 = lds64_a2(rg8 + 192 + 8 * n);
+      const uint2 s = lds64_a2(sm, rg + 192 + 8 * n);
+      const uint2 s8 = lds64_a2(sm, rg8 + 192 + 8 * n);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint32_t A = lds32_a2(rg + 64 * n + 16 * h + 4 * t);
-        const uint32_t B = lds32_a2(rg + 64 * n + 32 + 16 * h + 4 * t);
-        const uint32_t C = lds32_a2(rg + 128 + 32 * n + 16 * h + 4 * t);
-        const uint32_t A8 = lds32_a2(rg8 + 64 * n + 16 * h + 4 * t);
-        const uint32_t B8 = lds32_a2(rg8 + 64 * n + 32 + 16 * h + 4 * t);
-        const uint32_t C8 = lds32_a2(rg8 + 128 + 32 * n + 16 * h + 4 * t);
+        const uint32_t A = lds32_a2(sm, qo + 64 * n + 16 * h);
+        const uint32_t B = lds32_a2(sm, qo + 64 * n + 32 + 16 * h);
+        const uint32_t C = lds32_a2(sm, qo + 128 + 32 * n + 16 * h);
+        const uint32_t A8 = lds32_a2(sm, qo8 + 64 * n + 16 * h);
+        const uint32_t B8 = lds32_a2(sm, qo8 + 64 * n + 32 + 16 * h);
+        const uint32_t C8 = lds32_a2(sm, qo8 + 128 + 32 * n + 16 * h);
         uint32_t q[4], q8[4];
         q[0] = (A & 0x0F0F0F0Fu) | ((C << 4) & 0x30303030u);
         q[1] = (B & 0x0F0F0F0Fu) | ((C << 2) & 0x30303030u);
@@ -182,36 +246,31 @@ struct MmaQ6K {
         q8[1] = (B8 & 0x0F0F0F0Fu) | ((C8 << 2) & 0x30303030u);
         q8[2] = ((A8 >> 4) & 0x0F0F0F0Fu) | (C8 & 0x30303030u);
         q8[3] = ((B8 >> 4) & 0x0F0F0F0Fu) | ((C8 >> 2) & 0x30303030u);
+        int sc[4], sc8[4];
+        sc[0] = scale_of<0>(s, h); sc[1] = scale_of<1>(s, h); sc[2] = scale_of<2>(s, h); sc[3] = scale_of<3>(s, h);
+        sc8[0] = scale_of<0>(s8, h); sc8[1] = scale_of<1>(s8, h); sc8[2] = scale_of<2>(s8, h);
+        sc8[3] = scale_of<3>(s8, h);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          // group elements 128n + 32k + 16h .. : sub-block 4n + k, half h
-          const uint32_t b = g < 3 ? lds32(xsl + (4 * n + k) * 96 + 16 * h) : 0u;
           int dd[4];
-          mma_k16_u8s8(q[k], q8[k], b, dd);
-          // scale index 8n + h + 2k: byte (h + 2k) of the pair of words s
-          const int si = h + 2 * k;
-          const uint32_t sw = si < 4 ? s.x : s.y, sw8 = si < 4 ? s8.x : s8.y;
-          const int sc = static_cast<int>(static_cast<int8_t>((sw >> (8 * (si & 3))) & 0xFFu));
-          const int sc8 = static_cast<int>(static_cast<int8_t>((sw8 >> (8 * (si & 3))) & 0xFFu));
-          acc[0] += sc * dd[0];
-          acc[1] += sc * dd[1];
-          acc[2] += sc8 * dd[2];
-          acc[3] += sc8 * dd[3];
-          // this thread carries the bias of one group in four: (k == t)
-          if (k == t) {
-            const float xg = xp.sum16[sbg * 16 + 8 * n + 2 * k + h];
-            bias = fmaf(static_cast<float>(sc), xg, bias);
-            bias8 = fmaf(static_cast<float>(sc8), xg, bias8);
-          }
+          mma_k16_u8s8(q[k], q8[k], xb.b[2 * (4 * n + k) + h], dd);
+          acc[0] += sc[k] * dd[0];
+          acc[1] += sc[k] * dd[1];
+          acc[2] += sc8[k] * dd[2];
+          acc[3] += sc8[k] * dd[3];
         }
+        // this thread carries the bias of group k == t
+        const int st = t == 0 ? sc[0] : (t == 1 ? sc[1] : (t == 2 ? sc[2] : sc[3]));
+        const int st8 = t == 0 ? sc8[0] : (t == 1 ? sc8[1] : (t == 2 ? sc8[2] : sc8[3]));
+        bias = fmaf(static_cast<float>(st), xb.xg[2 * n + h], bias);
+        bias8 = fmaf(static_cast<float>(st8), xb.xg[2 * n + h], bias8);
       }
     }
-    const float sx = xp.scale[sbg];
-    const float d = f16_to_f32(lds16(rg + 208)), d8 = f16_to_f32(lds16(rg8 + 208));
+    const float d = f16_to_f32(lds16(sm, rg + 208)), d8 = f16_to_f32(lds16(sm, rg8 + 208));
     const float main = static_cast<float>(acc[0]) * w0 + static_cast<float>(acc[1]) * w1;
     const float main8 = static_cast<float>(acc[2]) * w0 + static_cast<float>(acc[3]) * w1;
-    pg += d * fmaf(sx, main, -32.0f * bias);
-    pg8 += d8 * fmaf(sx, main8, -32.0f * bias8);
+    pg += d * fmaf(xb.sx, main, -32.0f * bias);
+    pg8 += d8 * fmaf(xb.sx, main8, -32.0f * bias8);
   }
 };
 
@@ -221,26 +280,34 @@ struct MmaQ6K {
 struct MmaQ80 {
   static constexpr int kSBBytes = 272;
 
-  __device__ static __forceinline__ void tile(const uint8_t* rg, const uint8_t* rg8, int sbg, const XPrep& xp, int g,
-                                              int t, float w0, float w1, float& pg, float& pg8) {
-    float f = 0.f, f8 = 0.f;
+  struct XB {
+    uint2 b[8];
+    float sx;
+  };
+
+  __device__ static __forceinline__ void load_x(const XPrep& xp, int sbg, int g, int t, XB& o) {
     const uint8_t* xsl = xp.sl + static_cast<size_t>(sbg) * 8 * 96 + g * 32 + 8 * t;
 #pragma unroll
+    for (int b = 0; b < 8; ++b) o.b[b] = g < 3 ? lds64(xsl + b * 96) : make_uint2(0u, 0u);
+    o.sx = xp.scale[sbg];
+  }
+
+  __device__ static __forceinline__ void tile(const uint8_t* sm, uint32_t rg, uint32_t rg8, const XB& xb, int t,
+                                              float w0, float w1, float& pg, float& pg8) {
+    float f = 0.f, f8 = 0.f;
+#pragma unroll
     for (int b = 0; b < 8; ++b) {
-      const uint8_t* p = rg + 34 * b;
-      const uint8_t* p8 = rg8 + 34 * b;
-      const uint2 q = lds64_a2(p + 2 + 8 * t);
-      const uint2 q8 = lds64_a2(p8 + 2 + 8 * t);
-      const uint2 bx = g < 3 ? lds64(xsl + b * 96) : make_uint2(0u, 0u);
+      const uint32_t p = rg + 34 * b, p8 = rg8 + 34 * b;
+      const uint2 q = lds64_a2(sm, p + 2 + 8 * t);
+      const uint2 q8 = lds64_a2(sm, p8 + 2 + 8 * t);
       int dd[4];
-      mma_k32_s8s8(q.x, q8.x, q.y, q8.y, bx.x, bx.y, dd);
-      const float d = f16_to_f32(lds16(p)), d8 = f16_to_f32(lds16(p8));
+      mma_k32_s8s8(q.x, q8.x, q.y, q8.y, xb.b[b].x, xb.b[b].y, dd);
+      const float d = f16_to_f32(lds16(sm, p)), d8 = f16_to_f32(lds16(sm, p8));
       f = fmaf(d, static_cast<float>(dd[0]) * w0 + static_cast<float>(dd[1]) * w1, f);
       f8 = fmaf(d8, static_cast<float>(dd[2]) * w0 + static_cast<float>(dd[3]) * w1, f8);
     }
-    const float sx = xp.scale[sbg];
-    pg = fmaf(sx, f, pg);
-    pg8 = fmaf(sx, f8, pg8);
+    pg = fmaf(xb.sx, f, pg);
+    pg8 = fmaf(xb.sx, f8, pg8);
   }
 };
 
@@ -252,41 +319,56 @@ struct MmaQ80 {
 struct MmaQ40 {
   static constexpr int kSBBytes = 144;
 
-  __device__ static __forceinline__ void tile(const uint8_t* rg, const uint8_t* rg8, int sbg, const XPrep& xp, int g,
-                                              int t, float w0, float w1, float& pg, float& pg8) {
-    float f = 0.f, f8 = 0.f, bias = 0.f, bias8 = 0.f;
+  struct XB {
+    uint32_t b0[8], b1[8];
+    float xs[2];  // sums of x over blocks t and t + 4 (this thread carries their bias)
+    float sx;
+  };
+
+  __device__ static __forceinline__ void load_x(const XPrep& xp, int sbg, int g, int t, XB& o) {
     const uint8_t* xsl = xp.sl + static_cast<size_t>(sbg) * 8 * 96 + g * 32 + 4 * t;
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
-      const uint8_t* p = rg + 18 * b;
-      const uint8_t* p8 = rg8 + 18 * b;
-      const uint32_t q = lds32_a2(p + 2 + 4 * t);
-      const uint32_t q8 = lds32_a2(p8 + 2 + 4 * t);
-      uint32_t b0 = 0u, b1 = 0u;
-      if (g < 3) {
-        b0 = lds32(xsl + b * 96);
-        b1 = lds32(xsl + b * 96 + 16);
-      }
+      o.b0[b] = g < 3 ? lds32(xsl + b * 96) : 0u;
+      o.b1[b] = g < 3 ? lds32(xsl + b * 96 + 16) : 0u;
+    }
+    o.xs[0] = xp.sum32[sbg * 8 + t];
+    o.xs[1] = xp.sum32[sbg * 8 + t + 4];
+    o.sx = xp.scale[sbg];
+  }
+
+  __device__ static __forceinline__ void tile(const uint8_t* sm, uint32_t rg, uint32_t rg8, const XB& xb, int t,
+                                              float w0, float w1, float& pg, float& pg8) {
+    float f = 0.f, f8 = 0.f, bias = 0.f, bias8 = 0.f;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const uint32_t p = rg + 18 * b, p8 = rg8 + 18 * b;
+      const uint32_t q = lds32_a2(sm, p + 2 + 4 * t);
+      const uint32_t q8 = lds32_a2(sm, p8 + 2 + 4 * t);
       int dd[4];
-      mma_k32_u8s8(q & 0x0F0F0F0Fu, q8 & 0x0F0F0F0Fu, (q >> 4) & 0x0F0F0F0Fu, (q8 >> 4) & 0x0F0F0F0Fu, b0, b1, dd);
-      const float d = f16_to_f32(lds16(p)), d8 = f16_to_f32(lds16(p8));
+      mma_k32_u8s8(q & 0x0F0F0F0Fu, q8 & 0x0F0F0F0Fu, (q >> 4) & 0x0F0F0F0Fu, (q8 >> 4) & 0x0F0F0F0Fu, xb.b0[b],
+                   xb.b1[b], dd);
+      const float d = f16_to_f32(lds16(sm, p)), d8 = f16_to_f32(lds16(sm, p8));
       f = fmaf(d, static_cast<float>(dd[0]) * w0 + static_cast<float>(dd[1]) * w1, f);
       f8 = fmaf(d8, static_cast<float>(dd[2]) * w0 + static_cast<float>(dd[3]) * w1, f8);
       if ((b & 3) == t) {  // this thread carries the bias of blocks t and t + 4
-        const float xs = xp.sum32[sbg * 8 + b];
-        bias = fmaf(d, xs, bias);
-        bias8 = fmaf(d8, xs, bias8);
+        bias = fmaf(d, xb.xs[b >> 2], bias);
+        bias8 = fmaf(d8, xb.xs[b >> 2], bias8);
       }
     }
-    const float sx = xp.scale[sbg];
-    pg += fmaf(sx, f, -8.0f * bias);
-    pg8 += fmaf(sx, f8, -8.0f * bias8);
+    pg += fmaf(xb.sx, f, -8.0f * bias);
+    pg8 += fmaf(xb.sx, f8, -8.0f * bias8);
   }
 };
 
 // ---------------------------------------------------------------- the kernel
-template <class F>
-__global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1) k_gemv_mma(const MmaArgs a) {
+// TPS 16-row tiles per stage; WK consumer warps per tile split its k-chunk of
+// at most 16 super-blocks, so a warp owns at most 16 / WK of them.
+template <class F, int TPS, int WK>
+__global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaArgs a) {
+  constexpr int NCW = WK * TPS;  // consumer warps
+  constexpr int SR = 16 * TPS;   // rows per stage
+  constexpr int MAXJ = 16 / WK;  // super-blocks per warp per stage
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -296,10 +378,10 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1) k_gemv_mma(const
   if (row_end > a.rows) row_end = a.rows;
   if (row0 >= row_end) return;  // uniform across the CTA
   const int nrows = static_cast<int>(row_end - row0);
-  const int ntiles = (nrows + 15) >> 4;
-  const int nst = ntiles * a.NKC;
+  const int ngroups = (nrows + SR - 1) / SR;
+  const int nst = ngroups * a.NKC;
 
-  float* red = reinterpret_cast<float*>(smem + a.off_red);  // [NS][16][8]
+  float* red = reinterpret_cast<float*>(smem + a.off_red);  // [NS][SR][WK]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
   uint64_t* empty = full + a.NS;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + a.NS);
@@ -307,7 +389,7 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1) k_gemv_mma(const
   if (tid == 0) {
     for (int s = 0; s < a.NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], NCW);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -319,43 +401,49 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1) k_gemv_mma(const
     uint64_t policy = 0;
     if (lane == 0) policy = l2_evict_first_policy();
     policy = __shfl_sync(0xFFFFFFFFu, policy, 0);
-    // Stage s = k-chunk (s % NKC) of 16-row tile (s / NKC); one bulk copy per row.
+    // Stage s = k-chunk (s % NKC) of row group (s / NKC): one bulk copy per
+    // CG consecutive rows (whole rows when CG > 1, since then NKC == 1).
+    const size_t stage_bytes = static_cast<size_t>(SR / a.CG) * a.GS;
     auto issue = [&](int s) {
-      const int tile = s / a.NKC, kc = s - tile * a.NKC;
-      const int rows_t = min(16, nrows - 16 * tile);
+      const int grp = s / a.NKC, kc = s - grp * a.NKC;
+      const int rows_g = min(SR, nrows - SR * grp);
       const int sb0 = kc * a.KC;
       const int seg = min(a.KC, a.NSB - sb0) * F::kSBBytes;
       const int b = s % a.NS;
-      if (lane == 0) mbar_arrive_expect_tx(&full[b], static_cast<uint32_t>(rows_t * seg));
+      if (lane == 0) mbar_arrive_expect_tx(&full[b], static_cast<uint32_t>(rows_g * seg));
       __syncwarp();
-      if (lane < rows_t) {
-        const long long row = row0 + 16 * tile + lane;
-        bulk_g2s(smem + static_cast<size_t>(b) * 16 * a.RS + static_cast<size_t>(lane) * a.RS,
-                 a.w + row * a.RB + static_cast<long long>(sb0) * F::kSBBytes, static_cast<uint32_t>(seg), &full[b],
-                 policy);
+      const int ncopies = (rows_g + a.CG - 1) / a.CG;
+      if (lane < ncopies) {
+        const int rows_c = min(a.CG, rows_g - a.CG * lane);
+        const long long row = row0 + SR * grp + a.CG * lane;
+        bulk_g2s(smem + b * stage_bytes + static_cast<size_t>(lane) * a.GS,
+                 a.w + row * a.RB + static_cast<long long>(sb0) * F::kSBBytes,
+                 static_cast<uint32_t>(rows_c * seg), &full[b], policy);
       }
     };
-    // Weights are never written by an earlier kernel: their stream starts
-    // before the grid dependency resolves.
-    const int pre = min(a.NS, nst);
+    // Weights are never written by an earlier kernel: the first PRE stages
+    // stream before the grid dependency resolves.  The rest wait for it, so
+    // that the consumers' loads of x do not queue behind the whole ring.
+    const int pre = min(min(a.PRE, a.NS), nst);
     for (int s = 0; s < pre; ++s) issue(s);
     grid_dep_wait();
     grid_dep_launch();
+    for (int s = pre; s < min(a.NS, nst); ++s) issue(s);
     int buf = 0;
     uint32_t ph = 0;
     bool ok = true;
     for (int s = 0; s < nst; ++s) {
       ok = mbar_wait_bounded(&empty[buf], ph, kMmaTimeoutNs, abort_flag);
       if (!ok) break;
-      const int tile = s / a.NKC;
-      if (s - tile * a.NKC == a.NKC - 1) {
-        const int rows_t = min(16, nrows - 16 * tile);
-        const float* rb = red + static_cast<size_t>(buf) * 16 * kConsumerWarps;
-        if (lane < rows_t) {
+      const int grp = s / a.NKC;
+      if (s - grp * a.NKC == a.NKC - 1) {
+        const int rows_g = min(SR, nrows - SR * grp);
+        const float* rb = red + static_cast<size_t>(buf) * SR * WK;
+        if (lane < rows_g) {
           float acc = 0.f;
 #pragma unroll
-          for (int w = 0; w < kConsumerWarps; ++w) acc += rb[lane * kConsumerWarps + w];
-          a.y[row0 + 16 * tile + lane] = acc;
+          for (int w = 0; w < WK; ++w) acc += rb[lane * WK + w];
+          a.y[row0 + SR * grp + lane] = acc;
         }
       }
       __syncwarp();
@@ -376,52 +464,70 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1) k_gemv_mma(const
 
   // -------------------------------------------------- consumer warps
   const int cw = warp - 1;
-  const int ctid = tid - 32;
+  const int ti = cw / WK, wk = cw % WK;  // tile within the stage, k-split index
   const int g = lane >> 2, t = lane & 3;
+  // Staged rows this thread's MMA rows g and g + 8 read.  With 4-row copy
+  // groups, MMA rows g = 0..3 (one half-warp) come from four different
+  // groups, whose 32-mod-128 stride puts their bytes in distinct banks.
+  const int rr = a.CG == 4 ? (g & 3) * 4 + (g >> 2) : g;
+  const int rr8 = a.CG == 4 ? (g & 3) * 4 + 2 + (g >> 2) : g + 8;
+  const uint32_t off_g = static_cast<uint32_t>((rr / a.CG) * a.GS + (rr % a.CG) * a.SEG);
+  const uint32_t off_g8 = static_cast<uint32_t>((rr8 / a.CG) * a.GS + (rr8 % a.CG) * a.SEG);
+  const uint32_t stage_bytes = static_cast<uint32_t>((SR / a.CG) * a.GS);
+  const uint32_t tile_bytes = static_cast<uint32_t>((16 / a.CG) * a.GS);
   uint8_t* xsl = smem + a.off_xsl;
   float* sum32 = reinterpret_cast<float*>(smem + a.off_sum32);
   float* sum16 = reinterpret_cast<float*>(smem + a.off_sum16);
   float* sxs = reinterpret_cast<float*>(smem + a.off_scale);
   grid_dep_wait();
-  // x -> per-super-block int8 slices and group sums (lane: 8 elements).
-  for (int sb = cw; sb < a.NSB; sb += kConsumerWarps) {
-    const float4* xp4 = reinterpret_cast<const float4*>(a.x + 256 * sb + 8 * lane);
-    const float4 v0 = __ldg(xp4), v1 = __ldg(xp4 + 1);
-    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    float amax = 0.f;
+  // x -> per-super-block int8 slices and group sums (lane: 8 elements).  Each
+  // warp prepares exactly the super-blocks it consumes (its share [j0, j1) of
+  // every k-chunk), so it never waits for another warp; with two tiles per
+  // stage the warp of tile 0 prepares and its tile-1 partner waits for it.
+  if (ti == 0) {
+    for (int kcp = 0; kcp < a.NKC; ++kcp) {
+      const int sb0p = kcp * a.KC;
+      const int nsbp = min(a.KC, a.NSB - sb0p);
+      for (int sb = sb0p + wk * nsbp / WK; sb < sb0p + (wk + 1) * nsbp / WK; ++sb) {
+        const float4* xp4 = reinterpret_cast<const float4*>(a.x + 256 * sb + 8 * lane);
+        const float4 v0 = __ldg(xp4), v1 = __ldg(xp4 + 1);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-    const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-    uint32_t s0[2] = {0u, 0u}, s1[2] = {0u, 0u}, s2[2] = {0u, 0u};
-    float part = 0.f;
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+        const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+        uint32_t s0[2] = {0u, 0u}, s1[2] = {0u, 0u}, s2[2] = {0u, 0u};
+        float part = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      part += v[i];
-      const float u = v[i] * inv;
-      const float q0 = rintf(u);
-      const float u1 = (u - q0) * 254.0f;
-      const float q1 = rintf(u1);
-      const float q2 = rintf((u1 - q1) * 254.0f);
-      const int sh = 8 * (i & 3);
-      s0[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q0)) & 0xFFu) << sh;
-      s1[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q1)) & 0xFFu) << sh;
-      s2[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q2)) & 0xFFu) << sh;
+        for (int i = 0; i < 8; ++i) {
+          part += v[i];
+          const float u = v[i] * inv;
+          const float q0 = rintf(u);
+          const float u1 = (u - q0) * 254.0f;
+          const float q1 = rintf(u1);
+          const float q2 = rintf((u1 - q1) * 254.0f);
+          const int sh = 8 * (i & 3);
+          s0[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q0)) & 0xFFu) << sh;
+          s1[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q1)) & 0xFFu) << sh;
+          s2[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q2)) & 0xFFu) << sh;
+        }
+        // lane covers elements 8*lane .. +8: sub-block j = lane / 4, offset 8 * (lane % 4)
+        uint8_t* dst = xsl + (static_cast<size_t>(sb) * 8 + (lane >> 2)) * 96 + 8 * (lane & 3);
+        *reinterpret_cast<uint2*>(dst) = make_uint2(s0[0], s0[1]);
+        *reinterpret_cast<uint2*>(dst + 32) = make_uint2(s1[0], s1[1]);
+        *reinterpret_cast<uint2*>(dst + 64) = make_uint2(s2[0], s2[1]);
+        const float p16 = part + __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+        if ((lane & 1) == 0) sum16[sb * 16 + (lane >> 1)] = p16;
+        const float p32 = p16 + __shfl_xor_sync(0xFFFFFFFFu, p16, 2);
+        if ((lane & 3) == 0) sum32[sb * 8 + (lane >> 2)] = p32;
+        if (lane == 0) sxs[sb] = amax > 0.f ? amax / 127.0f : 0.f;
+      }
     }
-    // lane covers elements 8*lane .. +8: sub-block j = lane / 4, offset 8 * (lane % 4)
-    uint8_t* dst = xsl + (static_cast<size_t>(sb) * 8 + (lane >> 2)) * 96 + 8 * (lane & 3);
-    *reinterpret_cast<uint2*>(dst) = make_uint2(s0[0], s0[1]);
-    *reinterpret_cast<uint2*>(dst + 32) = make_uint2(s1[0], s1[1]);
-    *reinterpret_cast<uint2*>(dst + 64) = make_uint2(s2[0], s2[1]);
-    float p16 = part + __shfl_xor_sync(0xFFFFFFFFu, part, 1);
-    if ((lane & 1) == 0) sum16[sb * 16 + (lane >> 1)] = p16;
-    const float p32 = p16 + __shfl_xor_sync(0xFFFFFFFFu, p16, 2);
-    if ((lane & 3) == 0) sum32[sb * 8 + (lane >> 2)] = p32;
-    if (lane == 0) sxs[sb] = amax > 0.f ? amax / 127.0f : 0.f;
   }
-  named_bar_sync(1, 32 * kConsumerWarps);
-  (void)ctid;
+  if (TPS > 1) named_bar_sync(1 + wk, 64);  // warps wk (tile 0) and WK + wk (tile 1)
+  __syncwarp();
 
   const XPrep xp{xsl, sum32, sum16, sxs};
   // Column weights of this thread's two accumulator columns (2t, 2t+1):
@@ -429,8 +535,11 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1) k_gemv_mma(const
   const float w0 = t == 0 ? 1.0f : (t == 1 ? 1.0f / 64516.0f : 0.f);
   const float w1 = t == 0 ? 1.0f / 254.0f : 0.f;
   float pg = 0.f, pg8 = 0.f;
-  int buf = 0, kc = 0, tile = 0;
+  int buf = 0, kc = 0, loaded_kc = -1;
   uint32_t ph = 0;
+  // x operands of this warp's (at most two) super-blocks of the current
+  // k-chunk; with one k-chunk per row they are loaded once for the kernel.
+  typename F::XB xb0, xb1;
   for (int s = 0; s < nst; ++s) {
     const bool ok = mbar_wait_bounded(&full[buf], ph, kMmaTimeoutNs, abort_flag);
     if (!ok) {
@@ -440,30 +549,35 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1) k_gemv_mma(const
       }
       return;
     }
-    const uint8_t* st = smem + static_cast<size_t>(buf) * 16 * a.RS;
+    const uint32_t st = static_cast<uint32_t>(buf) * stage_bytes + static_cast<uint32_t>(ti) * tile_bytes;
     const int sb0 = kc * a.KC;
     const int nsb = min(a.KC, a.NSB - sb0);
-    const int j0 = cw * nsb / kConsumerWarps, j1 = (cw + 1) * nsb / kConsumerWarps;
-    const uint8_t* rg = st + static_cast<size_t>(g) * a.RS;
-    const uint8_t* rg8 = st + static_cast<size_t>(g + 8) * a.RS;
-    for (int j = j0; j < j1; ++j)
-      F::tile(rg + j * F::kSBBytes, rg8 + j * F::kSBBytes, sb0 + j, xp, g, t, w0, w1, pg, pg8);
+    const int j0 = wk * nsb / WK, j1 = (wk + 1) * nsb / WK;  // at most MAXJ (KC <= 16)
+    if (kc != loaded_kc) {
+      if (j0 < j1) F::load_x(xp, sb0 + j0, g, t, xb0);
+      if (MAXJ > 1 && j0 + 1 < j1) F::load_x(xp, sb0 + j0 + 1, g, t, xb1);
+      loaded_kc = kc;
+    }
+    const uint32_t rg = st + off_g + static_cast<uint32_t>(j0 * F::kSBBytes);
+    const uint32_t rg8 = st + off_g8 + static_cast<uint32_t>(j0 * F::kSBBytes);
+    if (j0 < j1) F::tile(smem, rg, rg8, xb0, t, w0, w1, pg, pg8);
+    if (MAXJ > 1 && j0 + 1 < j1) F::tile(smem, rg + F::kSBBytes, rg8 + F::kSBBytes, xb1, t, w0, w1, pg, pg8);
     if (kc == a.NKC - 1) {
       pg += __shfl_xor_sync(0xFFFFFFFFu, pg, 1);
       pg += __shfl_xor_sync(0xFFFFFFFFu, pg, 2);
       pg8 += __shfl_xor_sync(0xFFFFFFFFu, pg8, 1);
       pg8 += __shfl_xor_sync(0xFFFFFFFFu, pg8, 2);
       if (t == 0) {
-        float* rb = red + static_cast<size_t>(buf) * 16 * kConsumerWarps;
-        rb[g * kConsumerWarps + cw] = pg;
-        rb[(g + 8) * kConsumerWarps + cw] = pg8;
+        float* rb = red + static_cast<size_t>(buf) * SR * WK;
+        rb[(16 * ti + rr) * WK + wk] = pg;
+        rb[(16 * ti + rr8) * WK + wk] = pg8;
       }
       pg = pg8 = 0.f;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[buf]);
     if (++buf == a.NS) { buf = 0; ph ^= 1u; }
-    if (++kc == a.NKC) { kc = 0; ++tile; }
+    if (++kc == a.NKC) kc = 0;
   }
 }
 
@@ -483,12 +597,12 @@ static cudaError_t set_smem_once(size_t smem) {
 }
 
 template <auto Kern>
-static cudaError_t launch_mma_kernel(const MmaArgs& a, int grid, size_t smem, cudaStream_t st, bool pdl) {
+static cudaError_t launch_mma_kernel(const MmaArgs& a, int grid, int threads, size_t smem, cudaStream_t st, bool pdl) {
   cudaError_t e = set_smem_once<Kern>(smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(32 * (kConsumerWarps + 1));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -509,12 +623,21 @@ int mma_sb_bytes(int fmt) {
   }
 }
 
-cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int grid, size_t smem, cudaStream_t st, bool pdl) {
+template <class F>
+static cudaError_t launch_mma_fmt(const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
+                                  bool pdl) {
+  if (wk == 16) return launch_mma_kernel<k_gemv_mma<F, 1, 16>>(a, grid, 32 * 17, smem, st, pdl);
+  if (tps == 2) return launch_mma_kernel<k_gemv_mma<F, 2, 8>>(a, grid, 32 * 17, smem, st, pdl);
+  return launch_mma_kernel<k_gemv_mma<F, 1, 8>>(a, grid, 32 * 9, smem, st, pdl);
+}
+
+cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
+                            bool pdl) {
   switch (fmt) {
-    case 12: return launch_mma_kernel<k_gemv_mma<MmaQ4K>>(a, grid, smem, st, pdl);
-    case 14: return launch_mma_kernel<k_gemv_mma<MmaQ6K>>(a, grid, smem, st, pdl);
-    case 8: return launch_mma_kernel<k_gemv_mma<MmaQ80>>(a, grid, smem, st, pdl);
-    case 2: return launch_mma_kernel<k_gemv_mma<MmaQ40>>(a, grid, smem, st, pdl);
+    case 12: return launch_mma_fmt<MmaQ4K>(a, tps, wk, grid, smem, st, pdl);
+    case 14: return launch_mma_fmt<MmaQ6K>(a, tps, wk, grid, smem, st, pdl);
+    case 8: return launch_mma_fmt<MmaQ80>(a, tps, wk, grid, smem, st, pdl);
+    case 2: return launch_mma_fmt<MmaQ40>(a, tps, wk, grid, smem, st, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -143,9 +143,16 @@ SHAPES = [
 KERNELS = {
     # tuning that selects each kernel where the shape allows it
     "mma": {},
+    "mma_2tile_kc8": {"mma_tps": 2, "mma_kc": 8},
+    "mma_2cta": {"mma_ctas": 2},
+    "mma_wk16": {"mma_wk": 16},
+    "mma_wk8": {"mma_wk": 8},
+    "mma_rowcopy": {"mma_cg": 1},
+    "mma_coresident": {"mma_coresident": 1, "mma_pre": 0},
     "stream": {"mma": 0},
     "generic": {"force_generic": 1},
 }
+DEFAULT_TUNING = {"mma": 1, "force_generic": 0, "mma_tps": 1, "mma_kc": 16, "mma_ctas": 1, "mma_wk": 0, "mma_cg": 4, "mma_coresident": 0, "mma_pre": 1}
 
 
 @pytest.fixture(params=list(KERNELS))
@@ -153,8 +160,8 @@ def kernel(request, m3):
     for k, v in KERNELS[request.param].items():
         m3.matvec_quant.set_tuning(k, v)
     yield request.param
-    m3.matvec_quant.set_tuning("mma", 1)
-    m3.matvec_quant.set_tuning("force_generic", 0)
+    for k, v in DEFAULT_TUNING.items():
+        m3.matvec_quant.set_tuning(k, v)
 
 
 @pytest.mark.parametrize("dtype", [2, 8, 12, 14])
