@@ -303,7 +303,7 @@ def run_ours(args) -> int:
     achieved = abytes / per_step_s / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": kind,
-                "traffic": committed_traffic("k_gemv_stream", WORKLOAD), "kernel": "k_gemv_stream<FmtQ4K>",
+                "traffic": committed_traffic("k_gemv_mma", WORKLOAD), "kernel": "k_gemv_mma<MmaQ4K>",
                 "algorithmic_bytes_per_launch": abytes}
 
     cpu = None
@@ -352,8 +352,8 @@ def ctypes_status(lib, device):
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100000)
+    ap.add_argument("--warmup", type=int, default=500)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
