@@ -152,6 +152,47 @@ M3G_API const uint8_t* m3g_offload_tensor_ptr(const m3g_offload* ctx, uint64_t t
 
 M3G_API void m3g_offload_destroy(m3g_offload* ctx);
 
+/* ---------------------------------------------------------------- multi-GPU row sharding */
+
+/* One process per GPU.  Rank r keeps output rows [r*RPR, min(out, (r+1)*RPR))
+ * of each tensor, RPR = ceil(out_dim / world); a matvec computes the local
+ * rows and one NCCL all-gather of the fp32 slices gives every rank the whole
+ * output.  No counterpart in the reference (it is single-host, single-CPU);
+ * this is the sharded form of the GpuOffload shape above. */
+typedef struct m3g_shard m3g_shard;
+
+/* Row partition of a tensor (pure host arithmetic): M3G_ENONE when rows do
+ * not hold whole blocks (in_dim % block != 0) or the dtype has no kernel. */
+M3G_API int m3g_shard_plan(uint32_t dtype, uint64_t in_dim, uint64_t out_dim, int world, int rank,
+                           uint64_t* row_begin, uint64_t* rows_local, uint64_t* rows_per_rank,
+                           uint64_t* byte_begin, uint64_t* byte_len);
+
+/* 128-byte NCCL unique id, made on one rank and shared with the others. */
+M3G_API int m3g_shard_unique_id(uint8_t* out128);
+
+/* Join the communicator; M3G_ETIMEOUT (communicator aborted) when it is not
+ * complete within timeout_s seconds, e.g. because a rank never joined. */
+M3G_API int m3g_shard_create(int device, int rank, int world, const uint8_t* id128, uint64_t max_in,
+                             uint64_t max_out, double timeout_s, m3g_shard** out);
+
+/* Keep this rank's rows of a full GGUF tensor (raw_len == quant_raw_len). */
+M3G_API int m3g_shard_upload(m3g_shard* ctx, uint64_t tidx, uint32_t dtype, const uint8_t* raw, uint64_t raw_len,
+                             uint64_t in_dim, uint64_t out_dim);
+
+/* Device x [batch][in_dim]; y holds batch*RPR*world floats.  batch == 1:
+ * y[0 .. out_dim) is the full output; batch > 1: y is [rank][b][RPR]. */
+M3G_API int m3g_shard_matvec_dev(m3g_shard* ctx, uint64_t tidx, const float* x, uint64_t batch, float* y,
+                                 void* stream);
+
+/* Host x [batch][in_dim] -> host y [batch][out_dim] on every rank. */
+M3G_API int m3g_shard_matvec(m3g_shard* ctx, uint64_t tidx, const float* x, uint64_t batch, uint64_t in_dim,
+                             uint64_t out_dim, float* y);
+
+M3G_API int m3g_shard_info(const m3g_shard* ctx, uint64_t tidx, uint64_t* row_begin, uint64_t* rows_local,
+                           uint64_t* rows_per_rank);
+M3G_API uint64_t m3g_shard_calls(const m3g_shard* ctx);
+M3G_API void m3g_shard_destroy(m3g_shard* ctx);
+
 /* ---------------------------------------------------------------- diagnostics */
 
 /* Error word the kernels of `device` set when a bounded wait gives up

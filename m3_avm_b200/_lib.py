@@ -53,6 +53,16 @@ SIGNATURES: dict[str, tuple] = {
     "m3g_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(_u32), ctypes.c_int]),
     "m3g_launch_count": (_u64, []),
     "m3g_set_tuning": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int64]),
+    "m3g_shard_plan": (ctypes.c_int, [_u32, _u64, _u64, ctypes.c_int, ctypes.c_int] + [ctypes.POINTER(_u64)] * 5),
+    "m3g_shard_unique_id": (ctypes.c_int, [_vp]),
+    "m3g_shard_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _u64, _u64, ctypes.c_double,
+                                        ctypes.POINTER(_vp)]),
+    "m3g_shard_upload": (ctypes.c_int, [_vp, _u64, _u32, _vp, _u64, _u64, _u64]),
+    "m3g_shard_matvec_dev": (ctypes.c_int, [_vp, _u64, _vp, _u64, _vp, _vp]),
+    "m3g_shard_matvec": (ctypes.c_int, [_vp, _u64, _vp, _u64, _u64, _u64, _vp]),
+    "m3g_shard_info": (ctypes.c_int, [_vp, _u64] + [ctypes.POINTER(_u64)] * 3),
+    "m3g_shard_calls": (_u64, [_vp]),
+    "m3g_shard_destroy": (None, [_vp]),
 }
 
 _lib = None

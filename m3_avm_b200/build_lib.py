@@ -52,7 +52,7 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
     cmd = [
         nvcc_path(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "--shared", "-Xcompiler", "-fPIC",
         "-Xcompiler", "-fvisibility=hidden", "-ccbin", gcc, "-I", INCLUDE, "-I", CSRC,
-        "-DM3G_BUILD_LIB", "-o", LIB + ".tmp", *sources(),
+        "-DM3G_BUILD_LIB", "-o", LIB + ".tmp", *sources(), "-lnccl",
     ]
     if verbose_ptxas:
         cmd[1:1] = ["-Xptxas", "-v"]

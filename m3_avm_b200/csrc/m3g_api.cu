@@ -364,6 +364,37 @@ struct DevBuf {
 
 }  // namespace
 
+// Entry points shared with the other translation units of the library.
+namespace m3g {
+int host_fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+bool block_geometry(uint32_t dtype, int* be, int* bb) {
+  FmtInfo f;
+  if (!fmt_info(dtype, f)) return false;
+  *be = f.be;
+  *bb = f.bb;
+  return true;
+}
+
+// y[out] = W x on `st` for device pointers, on `device` (the current one).
+int gemv_device(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, float* y,
+                long long in_dim, long long out_dim, cudaStream_t st) {
+  FmtInfo f;
+  if (int rc = gemv_rules(dtype, raw_len, static_cast<uint64_t>(in_dim), static_cast<uint64_t>(out_dim), f)) return rc;
+  DevState* ds = nullptr;
+  if (int rc = dev_state(device, &ds)) return rc;
+  return gemv_launch(*ds, f, w, x, y, in_dim, out_dim, st);
+}
+}  // namespace m3g
+
 // ================================================================ C ABI
 extern "C" {
 

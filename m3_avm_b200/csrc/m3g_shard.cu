@@ -1,0 +1,317 @@
+// m3g_shard.cu -- output-row sharding of a GEMV across the GPUs of one node.
+//
+// Each rank (one process per GPU) keeps rows [r*RPR, min(out, (r+1)*RPR)) of
+// a weight tensor resident, RPR = ceil(out_dim / world).  A matvec computes
+// the local rows with the single-GPU kernels straight into this rank's slot
+// of a gather buffer, then one NCCL all-gather (in place) gives every rank
+// the full fp32 output.  This is the only collective of the path.
+//
+// Communicator creation is non-blocking with a wall-clock limit: a rank that
+// never joins makes create() abort the communicator and return M3G_ETIMEOUT
+// instead of hanging.
+#include <chrono>
+#include <cstring>
+#include <thread>
+#include <unordered_map>
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include "../../include/m3gemv.h"
+#include "m3g_internal.h"
+
+namespace m3g {
+int host_fail(int code, const char* fmt, ...);
+int gemv_device(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, float* y,
+                long long in_dim, long long out_dim, cudaStream_t st);
+bool block_geometry(uint32_t dtype, int* be, int* bb);
+}  // namespace m3g
+
+namespace {
+
+struct ShardTensor {
+  uint32_t dtype = 0;
+  uint64_t in_dim = 0, out_dim = 0;
+  uint64_t rpr = 0, row_begin = 0, rows_local = 0;
+  uint64_t bytes_local = 0;
+  uint8_t* d_raw = nullptr;
+};
+
+int nccl_fail(ncclResult_t r, const char* what) {
+  return m3g::host_fail(M3G_ENCCL, "%s: %s", what, ncclGetErrorString(r));
+}
+
+// The communicator is non-blocking (so that a missing rank cannot hang
+// creation): a call may return ncclInProgress, which is completed here by
+// polling the communicator's state for at most timeout_s seconds.
+int nccl_settle(ncclComm_t comm, ncclResult_t r, const char* what, double timeout_s) {
+  if (r == ncclSuccess) return M3G_OK;
+  if (r != ncclInProgress) return nccl_fail(r, what);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclInProgress;
+    if (ncclCommGetAsyncError(comm, &st) != ncclSuccess) return nccl_fail(ncclInternalError, what);
+    if (st == ncclSuccess) return M3G_OK;
+    if (st != ncclInProgress) return nccl_fail(st, what);
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s)
+      return m3g::host_fail(M3G_ETIMEOUT, "%s did not complete within %.1f s", what, timeout_s);
+    std::this_thread::yield();
+  }
+}
+
+}  // namespace
+
+struct m3g_shard {
+  int device = 0, rank = 0, world = 1;
+  ncclComm_t comm = nullptr;
+  cudaStream_t stream = nullptr;
+  uint64_t max_in = 0, max_out = 0;
+  std::unordered_map<uint64_t, ShardTensor> tensors;
+  float* d_x = nullptr;    // [batch][max_in]
+  float* d_ws = nullptr;   // gather buffer [world][batch][RPR]
+  uint64_t cap_x = 0, cap_ws = 0;
+  uint64_t calls = 0;
+  double timeout_s = 60.0;
+};
+
+namespace {
+
+struct Dev {
+  int prev = -1;
+  explicit Dev(int d) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(d);
+  }
+  ~Dev() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+int grow(float** p, uint64_t* cap, uint64_t n) {
+  if (n <= *cap) return M3G_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  cudaError_t e = cudaMalloc(p, n * sizeof(float));
+  if (e != cudaSuccess) return m3g::host_fail(M3G_ENOMEM, "shard buffer: %s", cudaGetErrorString(e));
+  *cap = n;
+  return M3G_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Row partition of a sharded tensor: pure host arithmetic, no device.
+int m3g_shard_plan(uint32_t dtype, uint64_t in_dim, uint64_t out_dim, int world, int rank, uint64_t* row_begin,
+                   uint64_t* rows_local, uint64_t* rows_per_rank, uint64_t* byte_begin, uint64_t* byte_len) {
+  int be = 0, bb = 0;
+  if (!m3g::block_geometry(dtype, &be, &bb)) return m3g::host_fail(M3G_ENONE, "shard: dtype %u has no fused kernel", dtype);
+  if (world < 1 || rank < 0 || rank >= world) return m3g::host_fail(M3G_EINVAL, "shard: rank %d of %d", rank, world);
+  if (in_dim == 0 || out_dim == 0) return m3g::host_fail(M3G_ENONE, "shard: zero dimension");
+  if (in_dim % static_cast<uint64_t>(be))
+    return m3g::host_fail(M3G_ENONE, "shard: rows must hold whole blocks (in_dim %% %d != 0)", be);
+  const uint64_t rb = in_dim / be * bb;
+  const uint64_t rpr = (out_dim + world - 1) / world;
+  const uint64_t b0 = std::min<uint64_t>(out_dim, rpr * rank);
+  const uint64_t b1 = std::min<uint64_t>(out_dim, rpr * (rank + 1));
+  if (row_begin) *row_begin = b0;
+  if (rows_local) *rows_local = b1 - b0;
+  if (rows_per_rank) *rows_per_rank = rpr;
+  if (byte_begin) *byte_begin = b0 * rb;
+  if (byte_len) *byte_len = (b1 - b0) * rb;
+  return M3G_OK;
+}
+
+int m3g_shard_unique_id(uint8_t* out128) {
+  if (!out128) return m3g::host_fail(M3G_EINVAL, "null id buffer");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  memcpy(out128, id.internal, NCCL_UNIQUE_ID_BYTES);
+  return M3G_OK;
+}
+
+int m3g_shard_create(int device, int rank, int world, const uint8_t* id128, uint64_t max_in, uint64_t max_out,
+                     double timeout_s, m3g_shard** out) {
+  if (!out || !id128) return m3g::host_fail(M3G_EINVAL, "null argument");
+  *out = nullptr;
+  if (world < 1 || rank < 0 || rank >= world) return m3g::host_fail(M3G_EINVAL, "rank %d of %d", rank, world);
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+    return m3g::host_fail(M3G_ECUDA, "no CUDA device %d", device);
+  Dev g(device);
+  auto* c = new m3g_shard();
+  c->device = device;
+  c->rank = rank;
+  c->world = world;
+  c->max_in = max_in;
+  c->max_out = max_out;
+  c->timeout_s = timeout_s;
+  ncclUniqueId id;
+  memcpy(id.internal, id128, NCCL_UNIQUE_ID_BYTES);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclResult_t r = ncclCommInitRankConfig(&c->comm, world, id, rank, &cfg);
+  const auto t0 = std::chrono::steady_clock::now();
+  while (r == ncclInProgress || (r == ncclSuccess && c->comm)) {
+    ncclResult_t st = ncclInProgress;
+    if (ncclCommGetAsyncError(c->comm, &st) != ncclSuccess) {
+      r = ncclInternalError;
+      break;
+    }
+    if (st == ncclSuccess) {
+      r = ncclSuccess;
+      break;
+    }
+    if (st != ncclInProgress) {
+      r = st;
+      break;
+    }
+    const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (dt > timeout_s) {
+      ncclCommAbort(c->comm);
+      delete c;
+      return m3g::host_fail(M3G_ETIMEOUT, "NCCL communicator init did not complete within %.1f s", timeout_s);
+    }
+    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+  }
+  if (r != ncclSuccess) {
+    if (c->comm) ncclCommAbort(c->comm);
+    delete c;
+    return nccl_fail(r, "ncclCommInitRankConfig");
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    ncclCommAbort(c->comm);
+    delete c;
+    return m3g::host_fail(M3G_ECUDA, "cudaStreamCreate: %s", cudaGetErrorString(e));
+  }
+  *out = c;
+  return M3G_OK;
+}
+
+void m3g_shard_destroy(m3g_shard* c) {
+  if (!c) return;
+  Dev g(c->device);
+  cudaStreamSynchronize(c->stream);
+  for (auto& kv : c->tensors) cudaFree(kv.second.d_raw);
+  if (c->d_x) cudaFree(c->d_x);
+  if (c->d_ws) cudaFree(c->d_ws);
+  if (c->comm) {
+    ncclResult_t r = ncclCommFinalize(c->comm);
+    if (nccl_settle(c->comm, r, "ncclCommFinalize", c->timeout_s) == M3G_OK) ncclCommDestroy(c->comm);
+    else ncclCommAbort(c->comm);
+  }
+  cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+// Keep this rank's rows of a full GGUF tensor resident.
+int m3g_shard_upload(m3g_shard* c, uint64_t tidx, uint32_t dtype, const uint8_t* raw, uint64_t raw_len,
+                     uint64_t in_dim, uint64_t out_dim) {
+  if (!c || !raw) return m3g::host_fail(M3G_EINVAL, "null argument");
+  uint64_t need = 0;
+  if (m3g_quant_raw_len(dtype, in_dim * out_dim, &need) != M3G_OK || need != raw_len)
+    return m3g::host_fail(M3G_ENONE, "shard upload: raw_len %llu != quant_raw_len %llu",
+                          static_cast<unsigned long long>(raw_len), static_cast<unsigned long long>(need));
+  ShardTensor t;
+  uint64_t b0 = 0;
+  if (int rc = m3g_shard_plan(dtype, in_dim, out_dim, c->world, c->rank, &t.row_begin, &t.rows_local, &t.rpr, &b0,
+                              &t.bytes_local))
+    return rc;
+  t.dtype = dtype;
+  t.in_dim = in_dim;
+  t.out_dim = out_dim;
+  Dev g(c->device);
+  cudaError_t e = cudaMalloc(&t.d_raw, t.bytes_local + 16);
+  if (e != cudaSuccess) return m3g::host_fail(M3G_ENOMEM, "shard upload: %s", cudaGetErrorString(e));
+  if (t.bytes_local) e = cudaMemcpy(t.d_raw, raw + b0, t.bytes_local, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(t.d_raw);
+    return m3g::host_fail(M3G_ECUDA, "shard upload copy: %s", cudaGetErrorString(e));
+  }
+  auto it = c->tensors.find(tidx);
+  if (it != c->tensors.end()) {
+    cudaStreamSynchronize(c->stream);
+    cudaFree(it->second.d_raw);
+    it->second = t;
+  } else {
+    c->tensors.emplace(tidx, t);
+  }
+  return M3G_OK;
+}
+
+// Y[b][out] for device x [b][in]: local rows, then one in-place all-gather.
+// y must hold batch * rows_per_rank * world floats; with batch == 1 the
+// result is y[0 .. out_dim), with batch > 1 it is y[rank][b][rows_per_rank]
+// (use m3g_shard_matvec for the [b][out] layout).
+int m3g_shard_matvec_dev(m3g_shard* c, uint64_t tidx, const float* x, uint64_t batch, float* y, void* stream) {
+  if (!c || !x || !y) return m3g::host_fail(M3G_EINVAL, "null argument");
+  auto it = c->tensors.find(tidx);
+  if (it == c->tensors.end()) return m3g::host_fail(M3G_ENOTFOUND, "tensor %llu not resident",
+                                                    static_cast<unsigned long long>(tidx));
+  const ShardTensor& t = it->second;
+  if (batch == 0) return M3G_OK;
+  Dev g(c->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  float* slot = y + static_cast<uint64_t>(c->rank) * batch * t.rpr;
+  if (t.rows_local) {
+    for (uint64_t b = 0; b < batch; ++b) {
+      int rc = m3g::gemv_device(c->device, t.dtype, t.d_raw, t.bytes_local, x + b * t.in_dim, slot + b * t.rpr,
+                                static_cast<long long>(t.in_dim), static_cast<long long>(t.rows_local), st);
+      if (rc) return rc;
+    }
+  }
+  ncclResult_t r = ncclAllGather(slot, y, batch * t.rpr, ncclFloat, c->comm, st);
+  if (int rc = nccl_settle(c->comm, r, "ncclAllGather", c->timeout_s)) return rc;
+  ++c->calls;
+  return M3G_OK;
+}
+
+// Host x [batch][in] -> host y [batch][out], full output on every rank.
+int m3g_shard_matvec(m3g_shard* c, uint64_t tidx, const float* x, uint64_t batch, uint64_t in_dim, uint64_t out_dim,
+                     float* y) {
+  if (!c || !x || !y) return m3g::host_fail(M3G_EINVAL, "null argument");
+  auto it = c->tensors.find(tidx);
+  if (it == c->tensors.end()) return m3g::host_fail(M3G_ENOTFOUND, "tensor %llu not resident",
+                                                    static_cast<unsigned long long>(tidx));
+  const ShardTensor& t = it->second;
+  if (t.in_dim != in_dim || t.out_dim != out_dim) return m3g::host_fail(M3G_ENONE, "shard matvec: dims differ");
+  if (batch == 0) return M3G_OK;
+  Dev g(c->device);
+  const uint64_t ws = static_cast<uint64_t>(c->world) * batch * t.rpr;
+  if (int rc = grow(&c->d_x, &c->cap_x, batch * in_dim)) return rc;
+  if (int rc = grow(&c->d_ws, &c->cap_ws, ws)) return rc;
+  cudaError_t e = cudaMemcpyAsync(c->d_x, x, batch * in_dim * sizeof(float), cudaMemcpyHostToDevice, c->stream);
+  if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard x copy: %s", cudaGetErrorString(e));
+  if (int rc = m3g_shard_matvec_dev(c, tidx, c->d_x, batch, c->d_ws, c->stream)) return rc;
+  // gather layout [rank][b][rpr] -> [b][out]
+  for (uint64_t b = 0; b < batch; ++b) {
+    for (int r = 0; r < c->world; ++r) {
+      const uint64_t r0 = std::min<uint64_t>(out_dim, t.rpr * r), r1 = std::min<uint64_t>(out_dim, t.rpr * (r + 1));
+      if (r1 <= r0) continue;
+      e = cudaMemcpyAsync(y + b * out_dim + r0, c->d_ws + (static_cast<uint64_t>(r) * batch + b) * t.rpr,
+                          (r1 - r0) * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
+      if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard y copy: %s", cudaGetErrorString(e));
+    }
+  }
+  e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard sync: %s", cudaGetErrorString(e));
+  return M3G_OK;
+}
+
+int m3g_shard_info(const m3g_shard* c, uint64_t tidx, uint64_t* row_begin, uint64_t* rows_local,
+                   uint64_t* rows_per_rank) {
+  if (!c) return m3g::host_fail(M3G_EINVAL, "null context");
+  auto it = c->tensors.find(tidx);
+  if (it == c->tensors.end()) return m3g::host_fail(M3G_ENOTFOUND, "tensor not resident");
+  if (row_begin) *row_begin = it->second.row_begin;
+  if (rows_local) *rows_local = it->second.rows_local;
+  if (rows_per_rank) *rows_per_rank = it->second.rpr;
+  return M3G_OK;
+}
+
+uint64_t m3g_shard_calls(const m3g_shard* c) { return c ? c->calls : 0; }
+
+}  // extern "C"
