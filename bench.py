@@ -341,6 +341,86 @@ def run_ours(args) -> int:
     return 0
 
 
+def run_lmhead(args) -> int:
+    """Vocab-head GEMV, Q6_K 128256 x 4096, rows sharded over the ranks plus one
+    NCCL all-gather of the fp32 logits (strong scaling: total work fixed)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from m3_avm_b200 import _lib, sharded, synth
+
+    in_dim, out_dim, dtype = 4096, 128256, 14
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        s = sharded.ShardedOffload.from_torch_dist(local, in_dim, out_dim, timeout_s=120)
+    else:
+        s = sharded.ShardedOffload(local, 0, 1, sharded.unique_id(), in_dim, out_dim, timeout_s=120)
+    lib = _lib.load()
+    raw = synth.weights(dtype, in_dim, out_dim, seed=1)
+    _, rows_local, rpr, _, bytes_local = sharded.shard_plan(dtype, in_dim, out_dim, world, rank)
+    props = torch.cuda.get_device_properties(dev)
+    l2 = getattr(props, "L2_cache_size", 126 * 1024 * 1024) or 126 * 1024 * 1024
+    n_copies = max(2, math.ceil(3 * l2 / max(bytes_local, 1)))
+    for c in range(n_copies):
+        if not s.upload(c, dtype, raw, in_dim, out_dim):
+            raise RuntimeError("shard upload failed: " + _lib.last_error())
+    x = torch.from_numpy(synth.activations(in_dim, seed=2)).to(dev)
+    y = torch.zeros(s.gather_len(0), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def replay():  # one pass over the weight copies, launched from the host
+        for c in range(n_copies):
+            s.matvec_dev(c, x, y, stream=stream.cuda_stream)
+
+    reps_w = max(1, args.warmup // n_copies)
+    reps = max(1, args.steps // n_copies)
+    for _ in range(reps_w):
+        replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.25)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(reps):
+        replay()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    steps = reps * n_copies
+    t = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    per_step = float(t.item()) / 1e3 / steps
+    ab = algorithmic_bytes(in_dim, out_dim, dtype)
+    peaks, kind = measured_peaks()
+    if rank == 0:
+        line = {
+            "metric": "Q6_K vocab-head GEMV + all-gather, effective GB/s @128256x4096", "value": round(ab / per_step / 1e9, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": reps_w * n_copies,
+            "ms_per_step": round(per_step * 1e3, 6), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "q6k_lmhead_128256x4096_sharded", "rows_per_rank": rpr, "weight_copies": n_copies,
+                       "parallelism": f"rows{world}+allgather", "l2": "inputs larger than L2 (rotating weight copies)"},
+            "per_gpu_hbm_gbs": round(bytes_local / per_step / 1e9, 2),
+            "pct_of_measured_hbm_peak_per_gpu": round(100 * bytes_local / per_step / 1e9 / float(peaks["hbm_gbs"]), 2),
+            "clocks": clocks,
+            "timing": "CUDA events around host-launched steps (GEMV + NCCL all-gather each), max over ranks",
+        }
+        print(json.dumps(line), flush=True)
+    s.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def ctypes_status(lib, device):
     import ctypes
 
@@ -359,10 +439,15 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-graph", action="store_true", help="launch each step from the host instead of a CUDA graph")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
+    ap.add_argument("--workload", choices=["gemv", "lmhead"], default="gemv",
+                    help="gemv: Q4_K 14336x4096 GEMV per GPU (the headline); "
+                         "lmhead: Q6_K 128256x4096 rows sharded over the GPUs + all-gather")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "lmhead":
+        return run_lmhead(args)
     return run_ours(args)
 
 

@@ -139,7 +139,8 @@ M3G_API int m3g_offload_matvec_batch(m3g_offload* ctx, uint64_t tidx, const floa
                              uint64_t out_dim, float* y);
 
 /* Device-resident form for callers that keep activations on the GPU:
- * x and y are device pointers, enqueued on `stream` (NULL = the context's own). */
+ * x and y are device pointers, enqueued on `stream` (NULL = the legacy
+ * default stream, like every other _dev entry point). */
 M3G_API int m3g_offload_matvec_dev(m3g_offload* ctx, uint64_t tidx, const float* x, uint64_t batch, float* y,
                            void* stream);
 

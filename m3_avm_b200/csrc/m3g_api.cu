@@ -755,7 +755,7 @@ int m3g_offload_create(int device, uint64_t max_in, uint64_t max_out, m3g_offloa
 void m3g_offload_destroy(m3g_offload* c) {
   if (!c) return;
   DeviceGuard g(c->device);
-  cudaStreamSynchronize(c->stream);
+  cudaDeviceSynchronize();
   for (auto& kv : c->tensors) cudaFree(kv.second.d_raw);
   free_io(c);
   cudaStreamDestroy(c->stream);
@@ -789,7 +789,7 @@ int m3g_offload_upload(m3g_offload* c, uint64_t tidx, uint32_t dtype, const uint
   }
   auto it = c->tensors.find(tidx);
   if (it != c->tensors.end()) {
-    cudaStreamSynchronize(c->stream);
+    cudaDeviceSynchronize();  // the old bytes may be in use on any stream
     cudaFree(it->second.d_raw);
     it->second = t;
   } else {
@@ -821,7 +821,7 @@ int m3g_offload_matvec_dev(m3g_offload* c, uint64_t tidx, const float* x, uint64
   DevState* ds = nullptr;
   if (int rc = dev_state(c->device, &ds)) return rc;
   DeviceGuard g(c->device);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL: the legacy default stream
   int rc = gemv_batch_launch(*ds, f, t.d_raw, x, y, static_cast<long long>(t.in_dim),
                              static_cast<long long>(t.out_dim), static_cast<long long>(batch), st);
   if (!rc) ++c->calls;

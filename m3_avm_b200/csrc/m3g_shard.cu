@@ -194,7 +194,7 @@ int m3g_shard_create(int device, int rank, int world, const uint8_t* id128, uint
 void m3g_shard_destroy(m3g_shard* c) {
   if (!c) return;
   Dev g(c->device);
-  cudaStreamSynchronize(c->stream);
+  cudaDeviceSynchronize();
   for (auto& kv : c->tensors) cudaFree(kv.second.d_raw);
   if (c->d_x) cudaFree(c->d_x);
   if (c->d_ws) cudaFree(c->d_ws);
@@ -233,7 +233,7 @@ int m3g_shard_upload(m3g_shard* c, uint64_t tidx, uint32_t dtype, const uint8_t*
   }
   auto it = c->tensors.find(tidx);
   if (it != c->tensors.end()) {
-    cudaStreamSynchronize(c->stream);
+    cudaDeviceSynchronize();  // the old bytes may be in use on any stream
     cudaFree(it->second.d_raw);
     it->second = t;
   } else {
@@ -254,7 +254,7 @@ int m3g_shard_matvec_dev(m3g_shard* c, uint64_t tidx, const float* x, uint64_t b
   const ShardTensor& t = it->second;
   if (batch == 0) return M3G_OK;
   Dev g(c->device);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL: the legacy default stream
   float* slot = y + static_cast<uint64_t>(c->rank) * batch * t.rpr;
   if (t.rows_local) {
     for (uint64_t b = 0; b < batch; ++b) {
