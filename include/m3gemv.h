@@ -194,6 +194,78 @@ M3G_API int m3g_shard_info(const m3g_shard* ctx, uint64_t tidx, uint64_t* row_be
 M3G_API uint64_t m3g_shard_calls(const m3g_shard* ctx);
 M3G_API void m3g_shard_destroy(m3g_shard* ctx);
 
+/* ---------------------------------------------------------------- fused GEMV forms of the decode step */
+
+/* y = W x' (+ res) on the tensor-core GEMV, with the input transform of the
+ * step that feeds it (device pointers, 16-byte aligned):
+ *   xmode 0: x' = x
+ *   xmode 1: x' = rms_norm_into(x, gamma) -- x / sqrt(mean(x^2) + 1e-5) * gamma,
+ *            src/inference.rs:1575-1585 (gamma NULL = ones)
+ *   xmode 2: x' = x * sigmoid(x) * x2 -- the SwiGLU product of
+ *            src/inference.rs:1092-1097 (x = gate, x2 = up)
+ *   res != NULL: y[j] = res[j] + (W x')[j], the residual adds of
+ *            src/inference.rs:1083 and :1103 (res may equal y).
+ * Needs in_dim % 256 == 0 and 16-byte rows (the tensor-core plan);
+ * M3G_EINVAL otherwise.  Enqueues on `stream` (NULL = legacy default stream). */
+M3G_API int m3g_matvec_fused_dev(const float* x, const float* x2, const float* gamma, const float* res, int xmode,
+                                 const uint8_t* raw, uint64_t raw_len, uint32_t dtype, uint64_t in_dim,
+                                 uint64_t out_dim, float* y, void* stream);
+
+/* ---------------------------------------------------------------- device-resident greedy decode
+ *
+ * RealInference::forward_one (src/inference.rs:953-1152) for a Llama-style
+ * model, every MATVEC on the fused kernels and no host round trip between
+ * tokens.  The engine owns one CUDA stream, the weights (uploaded once, GGUF
+ * bytes), a compact KV cache of max_pos positions and the token stream.
+ *
+ * Tensor slots: 0 token_embd (vocab x hidden; F32, F16 or a block dtype),
+ * 1 output_norm (f32[hidden]), 2 output (vocab x hidden), then nine per
+ * layer l at 3 + 9*l: attn_norm (f32), attn_q (hidden x hidden), attn_k and
+ * attn_v (n_kv_heads*head_dim x hidden), attn_output (hidden x hidden),
+ * ffn_norm (f32), ffn_gate and ffn_up (ffn x hidden), ffn_down (hidden x ffn).
+ * Matrices are out x in with in fastest (the GGUF orientation); head_dim =
+ * hidden / n_heads must be 64 or 128; hidden and ffn multiples of 256.
+ *
+ * Greedy sampling is sample_with_params (src/inference.rs:1315-1369) with
+ * top_k = 1: the lowest index holding the largest logit. */
+typedef struct m3g_decoder m3g_decoder;
+
+typedef struct {
+    uint64_t n_layers, hidden, ffn, n_heads, n_kv_heads, vocab, max_pos;
+    float rope_theta;
+} m3g_decoder_config;
+
+M3G_API int m3g_decoder_create(int device, const m3g_decoder_config* cfg, m3g_decoder** out);
+/* Copies one tensor to HBM (replacing an earlier upload of the slot). */
+M3G_API int m3g_decoder_upload(m3g_decoder* dec, uint32_t slot, uint32_t dtype, const void* raw, uint64_t raw_len);
+/* forward_one(token): one step at the current position; vocab logits to the
+ * host when `logits` is not NULL.  Replaces RealInference::forward_one. */
+M3G_API int m3g_decoder_forward(m3g_decoder* dec, uint32_t token, float* logits);
+/* prefill_logits (src/inference.rs:1388-1399): n steps over the prompt; the
+ * last step's logits to the host when `logits` is not NULL.  Afterwards the
+ * greedy pick of those logits is pending as the next token. */
+M3G_API int m3g_decoder_prefill(m3g_decoder* dec, const uint32_t* tokens, uint64_t n, float* logits);
+/* Greedy generation after a prefill or forward: out_tokens[0] is the pending
+ * pick, each of the next n_gen - 1 steps feeds the previous pick and picks
+ * the next.  All on the device; returns when the tokens are on the host. */
+M3G_API int m3g_decoder_generate(m3g_decoder* dec, uint64_t n_gen, uint32_t* out_tokens);
+/* Enqueues n_steps greedy steps without waiting (for timing); m3g_decoder_sync
+ * waits and reports kernel status. */
+M3G_API int m3g_decoder_run_async(m3g_decoder* dec, uint64_t n_steps);
+M3G_API int m3g_decoder_sync(m3g_decoder* dec);
+/* Token stream entries [first, first + n) (prompt tokens and greedy picks). */
+M3G_API int m3g_decoder_tokens(const m3g_decoder* dec, uint64_t first, uint64_t n, uint32_t* out);
+/* Positions held in the KV cache. */
+M3G_API uint64_t m3g_decoder_pos(const m3g_decoder* dec);
+/* truncate_kv_cache: keep the first n positions (0 clears the cache). */
+M3G_API int m3g_decoder_truncate(m3g_decoder* dec, uint64_t n);
+/* Device logits of the last step and the engine's stream (a cudaStream_t). */
+M3G_API const float* m3g_decoder_logits_dev(const m3g_decoder* dec);
+M3G_API void* m3g_decoder_stream(const m3g_decoder* dec);
+/* 1 (default): replay each step from a captured CUDA graph; 0: launch eagerly. */
+M3G_API int m3g_decoder_set_graph(m3g_decoder* dec, int use_graph);
+M3G_API void m3g_decoder_destroy(m3g_decoder* dec);
+
 /* ---------------------------------------------------------------- diagnostics */
 
 /* Error word the kernels of `device` set when a bounded wait gives up

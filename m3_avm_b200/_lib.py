@@ -27,6 +27,14 @@ _u64 = ctypes.c_uint64
 _u32 = ctypes.c_uint32
 _vp = ctypes.c_void_p
 
+
+
+class DecoderConfig(ctypes.Structure):
+    """m3g_decoder_config."""
+    _fields_ = [("n_layers", _u64), ("hidden", _u64), ("ffn", _u64), ("n_heads", _u64), ("n_kv_heads", _u64),
+                ("vocab", _u64), ("max_pos", _u64), ("rope_theta", ctypes.c_float)]
+
+
 # name -> (restype, argtypes); the list every test checks against the header.
 SIGNATURES: dict[str, tuple] = {
     "m3g_abi_version": (ctypes.c_int, []),
@@ -63,6 +71,21 @@ SIGNATURES: dict[str, tuple] = {
     "m3g_shard_info": (ctypes.c_int, [_vp, _u64] + [ctypes.POINTER(_u64)] * 3),
     "m3g_shard_calls": (_u64, [_vp]),
     "m3g_shard_destroy": (None, [_vp]),
+    "m3g_matvec_fused_dev": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, _vp, _u64, _u32, _u64, _u64, _vp, _vp]),
+    "m3g_decoder_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(DecoderConfig), ctypes.POINTER(_vp)]),
+    "m3g_decoder_upload": (ctypes.c_int, [_vp, _u32, _u32, _vp, _u64]),
+    "m3g_decoder_forward": (ctypes.c_int, [_vp, _u32, _vp]),
+    "m3g_decoder_prefill": (ctypes.c_int, [_vp, _vp, _u64, _vp]),
+    "m3g_decoder_generate": (ctypes.c_int, [_vp, _u64, _vp]),
+    "m3g_decoder_run_async": (ctypes.c_int, [_vp, _u64]),
+    "m3g_decoder_sync": (ctypes.c_int, [_vp]),
+    "m3g_decoder_tokens": (ctypes.c_int, [_vp, _u64, _u64, _vp]),
+    "m3g_decoder_pos": (_u64, [_vp]),
+    "m3g_decoder_truncate": (ctypes.c_int, [_vp, _u64]),
+    "m3g_decoder_logits_dev": (_vp, [_vp]),
+    "m3g_decoder_stream": (_vp, [_vp]),
+    "m3g_decoder_set_graph": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "m3g_decoder_destroy": (None, [_vp]),
 }
 
 _lib = None

@@ -141,7 +141,7 @@ int current_dev_state(DevState** out) {
 
 // ---------------------------------------------------------------- GEMV planning
 struct StreamPlan {
-  m3g::StreamArgs a;
+  m3g::StreamArgs a{};
   int threads = 0, grid = 0, upt = 0;
   size_t smem = 0;
 };
@@ -205,14 +205,13 @@ bool plan_stream(const FmtInfo& f, long long in_dim, long long rows, const uint8
 }
 
 struct MmaPlan {
-  m3g::MmaArgs a;
+  m3g::MmaArgs a{};
   int grid = 0, tps = 1, wk = 8;
   size_t smem = 0;
 };
 
 bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t* w, const float* x,
-              const DevState& ds, MmaPlan& p) {
-  if (g_tune.force_generic || !g_tune.mma) return false;
+              const DevState& ds, MmaPlan& p, bool coresident) {
   if (in_dim % 256) return false;
   const long long NSB = in_dim / 256;
   const int sbb = m3g::mma_sb_bytes(f.fmt);
@@ -243,7 +242,7 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   const long long mctas = std::max<int64_t>(1, g_tune.mma_ctas);
   // mma_coresident sizes a CTA for half an SM without changing the grid, so
   // the next GEMV's CTAs (launched early by PDL) fit beside this one's.
-  const long long div = std::max<long long>(mctas, g_tune.mma_coresident ? 2 : 1);
+  const long long div = std::max<long long>(mctas, coresident ? 2 : 1);
   const long long budget = std::min<long long>(ds.smem_optin, ds.smem_per_sm / div - 1024);
   const long long SR = 16 * tps;
   const long long per_stage = SR / CG * GS + SR * wk * 4 + 16;
@@ -287,7 +286,7 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
 int gemv_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const float* x, float* y,
                 long long in_dim, long long out_dim, cudaStream_t st) {
   MmaPlan mp;
-  if (plan_mma(f, in_dim, out_dim, w, x, ds, mp)) {
+  if (!g_tune.force_generic && g_tune.mma && plan_mma(f, in_dim, out_dim, w, x, ds, mp, g_tune.mma_coresident != 0)) {
     mp.a.w = w;
     mp.a.x = x;
     mp.a.y = y;
@@ -382,6 +381,46 @@ bool block_geometry(uint32_t dtype, int* be, int* bb) {
   *be = f.be;
   *bb = f.bb;
   return true;
+}
+
+int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
+               const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
+               cudaStream_t st, bool coresident) {
+  FmtInfo f;
+  if (int rc = gemv_rules(dtype, raw_len, static_cast<uint64_t>(in_dim), static_cast<uint64_t>(out_dim), f)) return rc;
+  if (xmode < kXPlain || xmode > kXSiluMul) return fail(M3G_EINVAL, "unknown input transform %d", xmode);
+  if (xmode == kXSiluMul && (!x2 || reinterpret_cast<uintptr_t>(x2) % 16))
+    return fail(M3G_EINVAL, "silu input needs a 16-byte aligned second vector");
+  if (gamma && reinterpret_cast<uintptr_t>(gamma) % 16) return fail(M3G_EINVAL, "norm weights not 16-byte aligned");
+  DevState* ds = nullptr;
+  if (int rc = dev_state(device, &ds)) return rc;
+  MmaPlan mp;
+  // A half-SM CTA needs two stages of the row segment; wide Q6_K rows may not
+  // fit, and then the CTA takes the whole SM.
+  const bool planned = plan_mma(f, in_dim, out_dim, w, x, *ds, mp, coresident) ||
+                       (coresident && plan_mma(f, in_dim, out_dim, w, x, *ds, mp, false));
+  if (!planned)
+    return fail(M3G_EINVAL, "no tensor-core plan for dtype %u, %lld x %lld (K %% 256, 16-byte rows and pointers)",
+                dtype, out_dim, in_dim);
+  mp.a.w = w;
+  mp.a.x = x;
+  mp.a.y = y;
+  mp.a.status = ds->status;
+  mp.a.x2 = x2;
+  mp.a.gamma = gamma;
+  mp.a.res = res;
+  mp.a.xmode = xmode;
+  cudaError_t e = launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "k_gemv_mma launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return M3G_OK;
+}
+
+int status_word(int device, uint32_t** out) {
+  DevState* ds = nullptr;
+  if (int rc = dev_state(device, &ds)) return rc;
+  *out = ds->status;
+  return M3G_OK;
 }
 
 // y[out] = W x on `st` for device pointers, on `device` (the current one).

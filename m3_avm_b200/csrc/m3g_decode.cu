@@ -1,0 +1,781 @@
+// m3g_decode.cu -- device-resident greedy decode of a Llama-style model.
+//
+// The decode step of RealInference::forward_one (src/inference.rs:953-1152)
+// with every MATVEC on the fused tensor-core GEMV, everything else on small
+// kernels, and no host round trip between tokens:
+//
+//   k_embed           token_embd row of tokens[pos] -> hidden (exact block decode)
+//   per layer:
+//     GEMV  qkv       rms_norm(hidden) * attn_norm, fused into the GEMV input;
+//                     q|k|v rows concatenated into one weight when they share a dtype
+//     k_attention     RoPE of q and k, K/V appended at pos, softmax attention
+//                     over positions [0, pos] per query head (GQA: head hh reads
+//                     KV head hh / (n_heads / n_kv_heads))
+//     GEMV  o         hidden += W_o att (residual fused in the epilogue)
+//     GEMV  gate|up   rms_norm(hidden) * ffn_norm input, gate|up rows concatenated
+//     GEMV  down      silu(gate) * up input, hidden += W_down (...)
+//   GEMV  head        rms_norm(hidden) * output_norm -> logits
+//   k_argmax_step     greedy token (lowest index of the largest logit) into
+//                     tokens[pos + 1] unless that slot holds a given prompt
+//                     token, then pos += 1
+//
+// The position and the token stream live in device memory, so one captured
+// CUDA graph replays every step; kernels chain with programmatic dependent
+// launch so each GEMV starts streaming its weights while the previous kernel
+// finishes.  The KV cache is compact (n_kv_heads * head_dim floats per
+// position and layer); the reference stores it repeated to the full hidden
+// width, which holds the same values.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/m3gemv.h"
+#include "m3g_device.cuh"
+#include "m3g_formats.cuh"
+#include "m3g_internal.h"
+
+namespace m3g {
+int host_fail(int code, const char* fmt, ...);
+bool block_geometry(uint32_t dtype, int* be, int* bb);
+}  // namespace m3g
+
+namespace m3g {
+namespace {
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+
+struct AttnArgs {
+  const float* qkv;   // [q: n_heads*HD][k: kvd][v: kvd]
+  float* kc;          // this layer's K cache [max_pos][kvd]
+  float* vc;          // this layer's V cache [max_pos][kvd]
+  const float* rope;  // [max_pos][HD/2][cos, sin]
+  const int* pos;
+  float* out;         // [n_heads*HD]
+  uint32_t* status;
+  int groups;         // n_heads / n_kv_heads
+  int kvd;            // n_kv_heads * HD
+  int qd;             // n_heads * HD
+  int max_pos;
+  float scale;        // 1 / sqrt(HD)
+};
+
+// One CTA per query head.  Scores use the reference's sequential dot product
+// (products and sums each rounded, in index order), so they are bit-identical
+// to it for identical q and k; the softmax sum and the weighted V sum are
+// reduced in a different order.
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
+  constexpr int HALF = HD / 2, DPL = HD / 32;
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                  // [HD] rotated q
+  float* kn = qs + HD;             // [HD] rotated k of this position
+  float* vn = kn + HD;             // [HD] v of this position
+  float* part = vn + HD;           // [warps][HD] partial outputs
+  float* red = part + kAttnWarps * HD;  // [64] reductions
+  float* sc = red + 64;            // [max_pos] scores, then weights
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hh = blockIdx.x, kv = hh / a.groups;
+  grid_dep_wait();
+  grid_dep_launch();
+  const int pos = *a.pos;
+  if (pos < 0 || pos >= a.max_pos) {
+    if (tid == 0) atomicOr(a.status, kStatusBadPos);
+    return;
+  }
+  const float* cs = a.rope + static_cast<size_t>(pos) * HD;
+  if (tid < HALF) {
+    const float c = cs[2 * tid], s = cs[2 * tid + 1];
+    const float* q = a.qkv + hh * HD;
+    const float* k = a.qkv + a.qd + kv * HD;
+    float x0 = q[tid], x1 = q[tid + HALF];
+    qs[tid] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    qs[tid + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    x0 = k[tid];
+    x1 = k[tid + HALF];
+    kn[tid] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    kn[tid + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+  } else if (tid < HALF + HD) {
+    vn[tid - HALF] = a.qkv[a.qd + a.kvd + kv * HD + tid - HALF];
+  }
+  __syncthreads();
+  // The first query head of each KV group appends this position's K and V;
+  // every head reads position pos from shared memory, so no CTA waits for it.
+  if (hh % a.groups == 0 && tid < HD) {
+    a.kc[static_cast<size_t>(pos) * a.kvd + kv * HD + tid] = kn[tid];
+    a.vc[static_cast<size_t>(pos) * a.kvd + kv * HD + tid] = vn[tid];
+  }
+  const int npos = pos + 1;
+  float lmax = -INFINITY;
+  for (int i = tid; i < npos; i += kAttnThreads) {
+    const float* kr = i == pos ? kn : a.kc + static_cast<size_t>(i) * a.kvd + kv * HD;
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < HD; j += 4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+      const float4 q4 = *reinterpret_cast<const float4*>(qs + j);
+      dot = __fadd_rn(dot, __fmul_rn(q4.x, k4.x));
+      dot = __fadd_rn(dot, __fmul_rn(q4.y, k4.y));
+      dot = __fadd_rn(dot, __fmul_rn(q4.z, k4.z));
+      dot = __fadd_rn(dot, __fmul_rn(q4.w, k4.w));
+    }
+    const float s = __fmul_rn(dot, a.scale);
+    sc[i] = s;
+    lmax = fmaxf(lmax, s);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xFFFFFFFFu, lmax, o));
+  if (lane == 0) red[warp] = lmax;
+  __syncthreads();
+  float mx = red[0];
+#pragma unroll
+  for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, red[w]);
+  float lsum = 0.f;
+  for (int i = tid; i < npos; i += kAttnThreads) {
+    const float e = expf(__fsub_rn(sc[i], mx));
+    sc[i] = e;
+    lsum += e;
+  }
+  lsum = warp_sum(lsum);
+  if (lane == 0) red[32 + warp] = lsum;
+  __syncthreads();
+  float sum = 0.f;
+#pragma unroll
+  for (int w = 0; w < kAttnWarps; ++w) sum += red[32 + w];
+  for (int i = tid; i < npos; i += kAttnThreads) sc[i] = __fdiv_rn(sc[i], sum);
+  __syncthreads();
+  float acc[DPL];
+#pragma unroll
+  for (int d = 0; d < DPL; ++d) acc[d] = 0.f;
+#pragma unroll 4
+  for (int i = warp; i < npos; i += kAttnWarps) {
+    const float w = sc[i];
+    const float* vr = (i == pos ? vn : a.vc + static_cast<size_t>(i) * a.kvd + kv * HD) + DPL * lane;
+    if (DPL == 2) {
+      const float2 v2 = *reinterpret_cast<const float2*>(vr);
+      acc[0] += w * v2.x;
+      acc[1] += w * v2.y;
+    } else {
+#pragma unroll
+      for (int d = 0; d < DPL; d += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(vr + d);
+        acc[d] += w * v4.x;
+        acc[d + 1] += w * v4.y;
+        acc[d + 2] += w * v4.z;
+        acc[d + 3] += w * v4.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int d = 0; d < DPL; ++d) part[warp * HD + DPL * lane + d] = acc[d];
+  __syncthreads();
+  if (tid < HD) {
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) o += part[w * HD + tid];
+    a.out[hh * HD + tid] = o;
+  }
+}
+
+// hidden = row tokens[pos] of the embedding, decoded exactly as the
+// reference's dequantize does (embedding_row, src/inference.rs:903-944).
+__global__ void __launch_bounds__(256) k_embed(const uint8_t* __restrict__ w, int dtype, int be, int bb,
+                                               const int* tokens, const int* pos, float* hidden, int h, int vocab,
+                                               int max_pos, uint32_t* status) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int p = *pos;
+  int tok = (p >= 0 && p < max_pos) ? tokens[p] : -1;
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(status, kStatusBadToken);
+    tok = 0;
+  }
+  const int e = blockIdx.x * 256 + threadIdx.x;
+  if (e >= h) return;
+  const long long idx = static_cast<long long>(tok) * h + e;
+  float v;
+  if (dtype == 0) {
+    v = reinterpret_cast<const float*>(w)[idx];
+  } else if (dtype == 1) {
+    v = __half2float(reinterpret_cast<const __half*>(w)[idx]);
+  } else {
+    const uint8_t* blk = w + (idx / be) * bb;
+    const int off = static_cast<int>(idx % be);
+    switch (dtype) {
+      case 14: v = q6k_elem(blk, off); break;
+      case 8: v = q8_0_elem(blk, off); break;
+      case 2: v = q4_0_elem(blk, off); break;
+      default: v = q4k_elem(blk, off); break;
+    }
+  }
+  hidden[e] = v;
+}
+
+// Greedy pick (sample_with_params with top_k = 1: the first index holding
+// the largest logit) and the step's bookkeeping.
+__global__ void __launch_bounds__(1024) k_argmax_step(const float* __restrict__ logits, int n, int* pos, int* tokens,
+                                                      const int* nfixed, int max_pos, int* last) {
+  __shared__ float bvs[32];
+  __shared__ int bis[32];
+  grid_dep_wait();
+  grid_dep_launch();
+  float bv = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  const int n4 = n / 4;
+  for (int i4 = threadIdx.x; i4 < n4; i4 += 1024) {
+    const float4 v = reinterpret_cast<const float4*>(logits)[i4];
+    const int i = 4 * i4;
+    if (v.x > bv) { bv = v.x; bi = i; }
+    if (v.y > bv) { bv = v.y; bi = i + 1; }
+    if (v.z > bv) { bv = v.z; bi = i + 2; }
+    if (v.w > bv) { bv = v.w; bi = i + 3; }
+  }
+  for (int i = 4 * n4 + threadIdx.x; i < n; i += 1024) {
+    const float v = logits[i];
+    if (v > bv) { bv = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+    const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) { bvs[warp] = bv; bis[warp] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 32; ++w)
+      if (bvs[w] > bv || (bvs[w] == bv && bis[w] < bi)) { bv = bvs[w]; bi = bis[w]; }
+    if (bi == 0x7FFFFFFF) bi = 0;  // every logit NaN
+    const int p = *pos, next = p + 1;
+    *last = bi;
+    if (next <= max_pos && next >= *nfixed) tokens[next] = bi;
+    *pos = next;
+  }
+}
+
+template <class Kern, class... Args>
+cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+}  // namespace
+}  // namespace m3g
+
+// ================================================================ engine
+namespace {
+
+using m3g::host_fail;
+
+#define DEC_CUDA(call)                                                                            \
+  do {                                                                                            \
+    cudaError_t e_ = (call);                                                                      \
+    if (e_ != cudaSuccess) return host_fail(M3G_ECUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr int kSlotEmbd = 0, kSlotOutNorm = 1, kSlotOut = 2, kSlotLayer0 = 3, kPerLayer = 9;
+enum { kAttnNorm = 0, kQ, kK, kV, kO, kFfnNorm, kGate, kUp, kDown };
+
+struct Tensor {
+  uint8_t* d = nullptr;  // device bytes (norms: f32)
+  uint64_t len = 0;
+  uint32_t dtype = 0;
+  int in = 0, out = 0;   // matrix shape; norms: in = out = hidden
+  bool set = false;
+};
+
+// A GEMV of the step: rows [0, out) of `w` (possibly several tensors' rows
+// concatenated) applied to in_dim inputs.
+struct Gemv {
+  const uint8_t* w = nullptr;
+  uint64_t len = 0;
+  uint32_t dtype = 0;
+  int in = 0, out = 0;
+};
+
+}  // namespace
+
+struct m3g_decoder {
+  int device = 0;
+  m3g_decoder_config cfg{};
+  int hd = 0, kvd = 0;
+  cudaStream_t st = nullptr;
+  std::vector<Tensor> t;
+  // Concatenated weights built at the first step (q|k|v and gate|up per layer).
+  std::vector<uint8_t*> fused;
+  std::vector<Gemv> qkv, gu;  // per layer; .w == nullptr: launch the parts separately
+  bool prepared = false;
+  // Activations and state.
+  float *hidden = nullptr, *qkvb = nullptr, *att = nullptr, *gub = nullptr, *logits = nullptr;
+  float *rope = nullptr, *kc = nullptr, *vc = nullptr;
+  int *dpos = nullptr, *tokens = nullptr, *nfixed = nullptr, *last = nullptr;
+  int* h_io = nullptr;  // pinned: [0] token / nfixed staging, [1] last token
+  uint32_t* status = nullptr;
+  int pos = 0;           // host mirror of the device position
+  bool pending = false;  // tokens[pos] holds the greedy pick of the last step
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  bool use_graph = true;
+  uint64_t steps = 0;
+};
+
+namespace {
+
+int slot_shape(const m3g_decoder* d, int slot, int* in, int* out, bool* is_norm) {
+  const int h = static_cast<int>(d->cfg.hidden), F = static_cast<int>(d->cfg.ffn);
+  *is_norm = false;
+  if (slot == kSlotEmbd || slot == kSlotOut) {
+    *in = h;
+    *out = static_cast<int>(d->cfg.vocab);
+    return M3G_OK;
+  }
+  if (slot == kSlotOutNorm) {
+    *in = *out = h;
+    *is_norm = true;
+    return M3G_OK;
+  }
+  const int kind = (slot - kSlotLayer0) % kPerLayer;
+  switch (kind) {
+    case kAttnNorm: case kFfnNorm: *in = *out = h; *is_norm = true; break;
+    case kQ: case kO: *in = h; *out = h; break;
+    case kK: case kV: *in = h; *out = d->kvd; break;
+    case kGate: case kUp: *in = h; *out = F; break;
+    default: *in = F; *out = h; break;
+  }
+  return M3G_OK;
+}
+
+bool gemv_dtype(uint32_t dt) { return dt == 2 || dt == 8 || dt == 12 || dt == 13 || dt == 14; }
+
+Gemv part(const Tensor& x) { return Gemv{x.d, x.len, x.dtype, x.in, x.out}; }
+
+// Concatenate the rows of tensors that share dtype and in_dim into one
+// weight so that a single GEMV launch covers them.
+int concat_rows(m3g_decoder* d, const std::vector<const Tensor*>& parts, Gemv& g) {
+  g = Gemv{};
+  for (const Tensor* p : parts)
+    if (p->dtype != parts[0]->dtype || p->in != parts[0]->in) return M3G_OK;  // launched separately
+  uint64_t total = 0;
+  int rows = 0;
+  for (const Tensor* p : parts) {
+    uint64_t need = 0;
+    if (m3g_quant_raw_len(p->dtype, static_cast<uint64_t>(p->in) * p->out, &need)) return M3G_OK;
+    if (need % 16) return M3G_OK;  // rows of the next part would start unaligned
+    total += need;
+    rows += p->out;
+  }
+  uint8_t* buf = nullptr;
+  DEC_CUDA(cudaMalloc(&buf, total));
+  d->fused.push_back(buf);
+  uint64_t off = 0;
+  for (const Tensor* p : parts) {
+    uint64_t need = 0;
+    m3g_quant_raw_len(p->dtype, static_cast<uint64_t>(p->in) * p->out, &need);
+    DEC_CUDA(cudaMemcpy(buf + off, p->d, need, cudaMemcpyDeviceToDevice));
+    off += need;
+  }
+  g = Gemv{buf, total, parts[0]->dtype, parts[0]->in, rows};
+  return M3G_OK;
+}
+
+int prepare(m3g_decoder* d) {
+  if (d->prepared) return M3G_OK;
+  for (size_t s = 0; s < d->t.size(); ++s)
+    if (!d->t[s].set) return host_fail(M3G_EINVAL, "decoder tensor slot %zu was never uploaded", s);
+  const int L = static_cast<int>(d->cfg.n_layers);
+  d->qkv.assign(L, Gemv{});
+  d->gu.assign(L, Gemv{});
+  for (int l = 0; l < L; ++l) {
+    const Tensor* T = &d->t[kSlotLayer0 + kPerLayer * l];
+    if (int rc = concat_rows(d, {&T[kQ], &T[kK], &T[kV]}, d->qkv[l])) return rc;
+    if (int rc = concat_rows(d, {&T[kGate], &T[kUp]}, d->gu[l])) return rc;
+  }
+  d->prepared = true;
+  return M3G_OK;
+}
+
+int gemv(m3g_decoder* d, const Gemv& g, const float* x, const float* x2, const float* gamma, const float* res,
+         int xmode, float* y) {
+  return m3g::gemv_fused(d->device, g.dtype, g.w, g.len, x, x2, gamma, res, xmode, y, g.in, g.out, d->st, true);
+}
+
+// Enqueue one decode step on d->st (also the body the graph captures).
+int enqueue_step(m3g_decoder* d) {
+  const int h = static_cast<int>(d->cfg.hidden), F = static_cast<int>(d->cfg.ffn);
+  const int L = static_cast<int>(d->cfg.n_layers), V = static_cast<int>(d->cfg.vocab);
+  const int mp = static_cast<int>(d->cfg.max_pos);
+  const Tensor& E = d->t[kSlotEmbd];
+  int be = 1, bb = 4;
+  if (E.dtype == 1) bb = 2;
+  else if (E.dtype != 0) m3g::block_geometry(E.dtype, &be, &bb);
+  DEC_CUDA(m3g::launch_pdl(m3g::k_embed, dim3((h + 255) / 256), dim3(256), 0, d->st, static_cast<const uint8_t*>(E.d),
+                           static_cast<int>(E.dtype), be, bb, static_cast<const int*>(d->tokens),
+                           static_cast<const int*>(d->dpos), d->hidden, h, V, mp, d->status));
+  const size_t attn_smem = sizeof(float) * (3 * d->hd + m3g::kAttnWarps * d->hd + 64 + static_cast<size_t>(mp));
+  for (int l = 0; l < L; ++l) {
+    const Tensor* T = &d->t[kSlotLayer0 + kPerLayer * l];
+    const float* g_attn = reinterpret_cast<const float*>(T[kAttnNorm].d);
+    const float* g_ffn = reinterpret_cast<const float*>(T[kFfnNorm].d);
+    if (d->qkv[l].w) {
+      if (int rc = gemv(d, d->qkv[l], d->hidden, nullptr, g_attn, nullptr, m3g::kXRmsNorm, d->qkvb)) return rc;
+    } else {
+      if (int rc = gemv(d, part(T[kQ]), d->hidden, nullptr, g_attn, nullptr, m3g::kXRmsNorm, d->qkvb)) return rc;
+      if (int rc = gemv(d, part(T[kK]), d->hidden, nullptr, g_attn, nullptr, m3g::kXRmsNorm, d->qkvb + h)) return rc;
+      if (int rc = gemv(d, part(T[kV]), d->hidden, nullptr, g_attn, nullptr, m3g::kXRmsNorm, d->qkvb + h + d->kvd))
+        return rc;
+    }
+    m3g::AttnArgs a{};
+    a.qkv = d->qkvb;
+    a.kc = d->kc + static_cast<size_t>(l) * mp * d->kvd;
+    a.vc = d->vc + static_cast<size_t>(l) * mp * d->kvd;
+    a.rope = d->rope;
+    a.pos = d->dpos;
+    a.out = d->att;
+    a.status = d->status;
+    a.groups = static_cast<int>(d->cfg.n_heads / d->cfg.n_kv_heads);
+    a.kvd = d->kvd;
+    a.qd = h;
+    a.max_pos = mp;
+    a.scale = 1.0f / sqrtf(static_cast<float>(d->hd));
+    const dim3 agrid(static_cast<unsigned>(d->cfg.n_heads));
+    if (d->hd == 64) {
+      DEC_CUDA(m3g::launch_pdl(m3g::k_attention<64>, agrid, dim3(m3g::kAttnThreads), attn_smem, d->st, a));
+    } else {
+      DEC_CUDA(m3g::launch_pdl(m3g::k_attention<128>, agrid, dim3(m3g::kAttnThreads), attn_smem, d->st, a));
+    }
+    if (int rc = gemv(d, part(T[kO]), d->att, nullptr, nullptr, d->hidden, m3g::kXPlain, d->hidden)) return rc;
+    if (d->gu[l].w) {
+      if (int rc = gemv(d, d->gu[l], d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, d->gub)) return rc;
+    } else {
+      if (int rc = gemv(d, part(T[kGate]), d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, d->gub)) return rc;
+      if (int rc = gemv(d, part(T[kUp]), d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, d->gub + F)) return rc;
+    }
+    if (int rc = gemv(d, part(T[kDown]), d->gub, d->gub + F, nullptr, d->hidden, m3g::kXSiluMul, d->hidden))
+      return rc;
+  }
+  const float* g_out = reinterpret_cast<const float*>(d->t[kSlotOutNorm].d);
+  if (int rc = gemv(d, part(d->t[kSlotOut]), d->hidden, nullptr, g_out, nullptr, m3g::kXRmsNorm, d->logits)) return rc;
+  DEC_CUDA(m3g::launch_pdl(m3g::k_argmax_step, dim3(1), dim3(1024), 0, d->st, static_cast<const float*>(d->logits), V,
+                           d->dpos, d->tokens, static_cast<const int*>(d->nfixed), mp, d->last));
+  return M3G_OK;
+}
+
+void drop_graph(m3g_decoder* d) {
+  if (d->exec) cudaGraphExecDestroy(d->exec);
+  if (d->graph) cudaGraphDestroy(d->graph);
+  d->exec = nullptr;
+  d->graph = nullptr;
+}
+
+// Run `n` steps.  The first step of a decoder runs eagerly (it also sets up
+// every kernel's shared-memory limit); later ones replay the captured graph.
+int run_steps(m3g_decoder* d, uint64_t n) {
+  if (int rc = prepare(d)) return rc;
+  if (d->pos + n > d->cfg.max_pos)
+    return host_fail(M3G_EINVAL, "%llu steps from position %d overflow the KV cache of %llu positions",
+                     static_cast<unsigned long long>(n), d->pos, static_cast<unsigned long long>(d->cfg.max_pos));
+  for (uint64_t i = 0; i < n; ++i) {
+    if (d->use_graph && d->steps > 0 && !d->exec) {
+      DEC_CUDA(cudaStreamBeginCapture(d->st, cudaStreamCaptureModeThreadLocal));
+      const int rc = enqueue_step(d);
+      cudaGraph_t g = nullptr;
+      const cudaError_t e = cudaStreamEndCapture(d->st, &g);
+      if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      if (e != cudaSuccess) return host_fail(M3G_ECUDA, "decode step capture: %s", cudaGetErrorString(e));
+      d->graph = g;
+      DEC_CUDA(cudaGraphInstantiate(&d->exec, d->graph, 0));
+    }
+    if (d->exec) {
+      DEC_CUDA(cudaGraphLaunch(d->exec, d->st));
+    } else if (int rc = enqueue_step(d)) {
+      return rc;
+    }
+    ++d->steps;
+    ++d->pos;
+  }
+  d->pending = true;
+  return M3G_OK;
+}
+
+int check_status(m3g_decoder* d) {
+  DEC_CUDA(cudaStreamSynchronize(d->st));
+  uint32_t s = 0;
+  DEC_CUDA(cudaMemcpy(&s, d->status, sizeof s, cudaMemcpyDeviceToHost));
+  if (s & (m3g::kStatusBadPos | m3g::kStatusBadToken | m3g::kStatusCopyTimeout)) {
+    cudaMemset(d->status, 0, sizeof s);
+    if (s & m3g::kStatusCopyTimeout) return host_fail(M3G_ETIMEOUT, "a staged weight copy did not complete in time");
+    return host_fail(M3G_EINVAL, "decode step saw %s", (s & m3g::kStatusBadPos) ? "a position outside the KV cache"
+                                                                             : "a token outside the vocabulary");
+  }
+  return M3G_OK;
+}
+
+struct DevGuard {
+  int prev = -1;
+  explicit DevGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~DevGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+M3G_API int m3g_decoder_create(int device, const m3g_decoder_config* cfg, m3g_decoder** out) {
+  if (!cfg || !out) return host_fail(M3G_EINVAL, "null argument");
+  *out = nullptr;
+  const m3g_decoder_config& c = *cfg;
+  if (!c.n_layers || !c.hidden || !c.ffn || !c.n_heads || !c.n_kv_heads || !c.vocab || !c.max_pos)
+    return host_fail(M3G_EINVAL, "zero dimension in the decoder shape");
+  if (c.hidden % c.n_heads || c.n_heads % c.n_kv_heads) return host_fail(M3G_EINVAL, "heads do not divide");
+  const uint64_t hd = c.hidden / c.n_heads;
+  if (hd != 64 && hd != 128) return host_fail(M3G_EINVAL, "head_dim %llu (64 and 128 are supported)",
+                                             static_cast<unsigned long long>(hd));
+  if (c.hidden % 256 || c.ffn % 256) return host_fail(M3G_EINVAL, "hidden and ffn must be multiples of 256");
+  if (c.vocab > (1u << 30) || c.max_pos > (1u << 20) || c.hidden > (1u << 16) || c.ffn > (1u << 20) ||
+      c.n_layers > 4096)
+    return host_fail(M3G_EINVAL, "decoder shape too large");
+  if (c.max_pos * sizeof(float) + 4096 > 200 * 1024)
+    return host_fail(M3G_EINVAL, "max_pos %llu exceeds the attention kernel's shared memory",
+                     static_cast<unsigned long long>(c.max_pos));
+  DevGuard g(device);
+  auto* d = new m3g_decoder();
+  d->device = device;
+  d->cfg = c;
+  d->hd = static_cast<int>(hd);
+  d->kvd = static_cast<int>(c.n_kv_heads * hd);
+  d->t.resize(kSlotLayer0 + kPerLayer * c.n_layers);
+  for (size_t s = 0; s < d->t.size(); ++s) {
+    bool norm = false;
+    slot_shape(d, static_cast<int>(s), &d->t[s].in, &d->t[s].out, &norm);
+  }
+  auto fail = [&](int rc) {
+    m3g_decoder_destroy(d);
+    return rc;
+  };
+  const size_t h = c.hidden, F = c.ffn, mp = c.max_pos;
+  if (int rc = m3g::status_word(device, &d->status)) return fail(rc);
+  cudaError_t e = cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&d->hidden, 4 * h);
+  if (e == cudaSuccess) e = cudaMalloc(&d->qkvb, 4 * (h + 2 * d->kvd));
+  if (e == cudaSuccess) e = cudaMalloc(&d->att, 4 * h);
+  if (e == cudaSuccess) e = cudaMalloc(&d->gub, 4 * 2 * F);
+  if (e == cudaSuccess) e = cudaMalloc(&d->logits, 4 * c.vocab);
+  if (e == cudaSuccess) e = cudaMalloc(&d->rope, 4 * mp * hd);
+  if (e == cudaSuccess) e = cudaMalloc(&d->kc, 4 * c.n_layers * mp * d->kvd);
+  if (e == cudaSuccess) e = cudaMalloc(&d->vc, 4 * c.n_layers * mp * d->kvd);
+  if (e == cudaSuccess) e = cudaMalloc(&d->dpos, 4 * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&d->tokens, 4 * (mp + 1));
+  if (e == cudaSuccess) e = cudaHostAlloc(&d->h_io, 4 * 4, cudaHostAllocDefault);
+  if (e != cudaSuccess) {
+    const int rc = host_fail(e == cudaErrorMemoryAllocation ? M3G_ENOMEM : M3G_ECUDA, "decoder setup: %s",
+                             cudaGetErrorString(e));
+    return fail(rc);
+  }
+  d->nfixed = d->dpos + 1;
+  d->last = d->dpos + 2;
+  // RoPE table: (cos, sin) of pos * theta^(-2i / head_dim) in f32, the
+  // arithmetic of src/inference.rs:1000-1007, computed once on the host.
+  std::vector<float> rope(mp * hd);
+  for (size_t p = 0; p < mp; ++p)
+    for (size_t i = 0; i < hd / 2; ++i) {
+      const float f = static_cast<float>(p) * powf(c.rope_theta, -2.0f * static_cast<float>(i) / static_cast<float>(hd));
+      rope[p * hd + 2 * i] = cosf(f);
+      rope[p * hd + 2 * i + 1] = sinf(f);
+    }
+  e = cudaMemcpy(d->rope, rope.data(), 4 * mp * hd, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(d->dpos, 0, 4 * 4);
+  if (e == cudaSuccess) e = cudaMemset(d->tokens, 0, 4 * (mp + 1));
+  if (e == cudaSuccess) {
+    const size_t attn_smem = sizeof(float) * (3 * hd + m3g::kAttnWarps * hd + 64 + mp);
+    e = hd == 64 ? cudaFuncSetAttribute(m3g::k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(attn_smem))
+                 : cudaFuncSetAttribute(m3g::k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(attn_smem));
+  }
+  if (e != cudaSuccess) return fail(host_fail(M3G_ECUDA, "decoder setup: %s", cudaGetErrorString(e)));
+  *out = d;
+  return M3G_OK;
+}
+
+M3G_API int m3g_decoder_upload(m3g_decoder* d, uint32_t slot, uint32_t dtype, const void* raw, uint64_t raw_len) {
+  if (!d || !raw) return host_fail(M3G_EINVAL, "null argument");
+  if (slot >= d->t.size()) return host_fail(M3G_EINVAL, "slot %u out of range", slot);
+  int in = 0, out = 0;
+  bool norm = false;
+  slot_shape(d, static_cast<int>(slot), &in, &out, &norm);
+  uint64_t need = 0;
+  if (norm) {
+    if (dtype != 0) return host_fail(M3G_EINVAL, "norm weights of slot %u must be f32 (dtype 0)", slot);
+    need = 4ull * in;
+  } else if (slot == kSlotEmbd && (dtype == 0 || dtype == 1)) {
+    need = (dtype == 0 ? 4ull : 2ull) * in * out;
+  } else {
+    if (!gemv_dtype(dtype)) return host_fail(M3G_EINVAL, "slot %u: dtype %u has no fused GEMV", slot, dtype);
+    if (m3g_quant_raw_len(dtype, static_cast<uint64_t>(in) * out, &need))
+      return host_fail(M3G_EINVAL, "slot %u: %d x %d is not whole blocks of dtype %u", slot, out, in, dtype);
+  }
+  if (raw_len < need)
+    return host_fail(M3G_EINVAL, "slot %u: %llu bytes, needs %llu", slot, static_cast<unsigned long long>(raw_len),
+                     static_cast<unsigned long long>(need));
+  DevGuard g(d->device);
+  if (cudaStreamSynchronize(d->st) != cudaSuccess) return host_fail(M3G_ECUDA, "decoder stream failed");
+  drop_graph(d);
+  for (uint8_t* f : d->fused) cudaFree(f);
+  d->fused.clear();
+  d->prepared = false;
+  Tensor& t = d->t[slot];
+  if (t.d) cudaFree(t.d);
+  t.d = nullptr;
+  t.set = false;
+  DEC_CUDA(cudaMalloc(&t.d, need));
+  DEC_CUDA(cudaMemcpy(t.d, raw, need, cudaMemcpyHostToDevice));
+  t.len = need;
+  t.dtype = dtype;
+  t.set = true;
+  return M3G_OK;
+}
+
+M3G_API int m3g_decoder_forward(m3g_decoder* d, uint32_t token, float* logits) {
+  if (!d) return host_fail(M3G_EINVAL, "null decoder");
+  if (token >= d->cfg.vocab) return host_fail(M3G_EINVAL, "token %u outside the vocabulary", token);
+  if (d->pos >= static_cast<int>(d->cfg.max_pos)) return host_fail(M3G_EINVAL, "KV cache full");
+  DevGuard g(d->device);
+  DEC_CUDA(cudaStreamSynchronize(d->st));
+  d->h_io[0] = static_cast<int>(token);
+  d->h_io[1] = 0;
+  DEC_CUDA(cudaMemcpyAsync(d->tokens + d->pos, &d->h_io[0], 4, cudaMemcpyHostToDevice, d->st));
+  DEC_CUDA(cudaMemcpyAsync(d->nfixed, &d->h_io[1], 4, cudaMemcpyHostToDevice, d->st));
+  if (int rc = run_steps(d, 1)) return rc;
+  if (logits) DEC_CUDA(cudaMemcpyAsync(logits, d->logits, 4 * d->cfg.vocab, cudaMemcpyDeviceToHost, d->st));
+  return check_status(d);
+}
+
+M3G_API int m3g_decoder_prefill(m3g_decoder* d, const uint32_t* tokens, uint64_t n, float* logits) {
+  if (!d || (!tokens && n)) return host_fail(M3G_EINVAL, "null argument");
+  if (n == 0) return M3G_OK;
+  if (d->pos + n > d->cfg.max_pos) return host_fail(M3G_EINVAL, "prompt overflows the KV cache");
+  for (uint64_t i = 0; i < n; ++i)
+    if (tokens[i] >= d->cfg.vocab) return host_fail(M3G_EINVAL, "token %u outside the vocabulary", tokens[i]);
+  DevGuard g(d->device);
+  DEC_CUDA(cudaStreamSynchronize(d->st));
+  DEC_CUDA(cudaMemcpy(d->tokens + d->pos, tokens, 4 * n, cudaMemcpyHostToDevice));
+  const int nfixed = d->pos + static_cast<int>(n);
+  DEC_CUDA(cudaMemcpy(d->nfixed, &nfixed, 4, cudaMemcpyHostToDevice));
+  if (int rc = run_steps(d, n)) return rc;
+  if (logits) DEC_CUDA(cudaMemcpyAsync(logits, d->logits, 4 * d->cfg.vocab, cudaMemcpyDeviceToHost, d->st));
+  return check_status(d);
+}
+
+M3G_API int m3g_decoder_generate(m3g_decoder* d, uint64_t n_gen, uint32_t* out_tokens) {
+  if (!d || (!out_tokens && n_gen)) return host_fail(M3G_EINVAL, "null argument");
+  if (n_gen == 0) return M3G_OK;
+  if (!d->pending) return host_fail(M3G_EINVAL, "generate needs a prefilled prompt (no step has run)");
+  if (d->pos + n_gen - 1 > d->cfg.max_pos) return host_fail(M3G_EINVAL, "generation overflows the KV cache");
+  DevGuard g(d->device);
+  const int first = d->pos;
+  if (int rc = run_steps(d, n_gen - 1)) return rc;
+  DEC_CUDA(cudaMemcpyAsync(out_tokens, d->tokens + first, 4 * n_gen, cudaMemcpyDeviceToHost, d->st));
+  return check_status(d);
+}
+
+M3G_API int m3g_decoder_run_async(m3g_decoder* d, uint64_t n_steps) {
+  if (!d) return host_fail(M3G_EINVAL, "null decoder");
+  if (n_steps && !d->pending) return host_fail(M3G_EINVAL, "run_async needs a prefilled prompt");
+  DevGuard g(d->device);
+  return run_steps(d, n_steps);
+}
+
+M3G_API int m3g_decoder_sync(m3g_decoder* d) {
+  if (!d) return host_fail(M3G_EINVAL, "null decoder");
+  DevGuard g(d->device);
+  return check_status(d);
+}
+
+M3G_API int m3g_decoder_tokens(const m3g_decoder* d, uint64_t first, uint64_t n, uint32_t* out) {
+  if (!d || (!out && n)) return host_fail(M3G_EINVAL, "null argument");
+  if (first + n > d->cfg.max_pos + 1) return host_fail(M3G_EINVAL, "token range outside the stream");
+  DevGuard g(d->device);
+  DEC_CUDA(cudaStreamSynchronize(d->st));
+  if (n) DEC_CUDA(cudaMemcpy(out, d->tokens + first, 4 * n, cudaMemcpyDeviceToHost));
+  return M3G_OK;
+}
+
+M3G_API uint64_t m3g_decoder_pos(const m3g_decoder* d) { return d ? static_cast<uint64_t>(d->pos) : 0; }
+
+M3G_API int m3g_decoder_truncate(m3g_decoder* d, uint64_t n) {
+  if (!d) return host_fail(M3G_EINVAL, "null decoder");
+  if (n > static_cast<uint64_t>(d->pos)) return host_fail(M3G_EINVAL, "cannot truncate forward");
+  DevGuard g(d->device);
+  DEC_CUDA(cudaStreamSynchronize(d->st));
+  const int p = static_cast<int>(n);
+  DEC_CUDA(cudaMemcpy(d->dpos, &p, 4, cudaMemcpyHostToDevice));
+  d->pos = p;
+  d->pending = false;
+  return M3G_OK;
+}
+
+M3G_API const float* m3g_decoder_logits_dev(const m3g_decoder* d) { return d ? d->logits : nullptr; }
+
+M3G_API void* m3g_decoder_stream(const m3g_decoder* d) { return d ? static_cast<void*>(d->st) : nullptr; }
+
+M3G_API int m3g_decoder_set_graph(m3g_decoder* d, int use_graph) {
+  if (!d) return host_fail(M3G_EINVAL, "null decoder");
+  DevGuard g(d->device);
+  DEC_CUDA(cudaStreamSynchronize(d->st));
+  drop_graph(d);
+  d->use_graph = use_graph != 0;
+  return M3G_OK;
+}
+
+M3G_API void m3g_decoder_destroy(m3g_decoder* d) {
+  if (!d) return;
+  DevGuard g(d->device);
+  if (d->st) cudaStreamSynchronize(d->st);
+  drop_graph(d);
+  for (Tensor& t : d->t)
+    if (t.d) cudaFree(t.d);
+  for (uint8_t* f : d->fused) cudaFree(f);
+  for (void* p : {static_cast<void*>(d->hidden), static_cast<void*>(d->qkvb), static_cast<void*>(d->att),
+                  static_cast<void*>(d->gub), static_cast<void*>(d->logits), static_cast<void*>(d->rope),
+                  static_cast<void*>(d->kc), static_cast<void*>(d->vc), static_cast<void*>(d->dpos),
+                  static_cast<void*>(d->tokens)})
+    if (p) cudaFree(p);
+  if (d->h_io) cudaFreeHost(d->h_io);
+  if (d->st) cudaStreamDestroy(d->st);
+  delete d;
+}
+
+// Fused GEMV with the decode step's input transforms and residual epilogue.
+M3G_API int m3g_matvec_fused_dev(const float* x, const float* x2, const float* gamma, const float* res, int xmode,
+                                 const uint8_t* raw, uint64_t raw_len, uint32_t dtype, uint64_t in_dim,
+                                 uint64_t out_dim, float* y, void* stream) {
+  if (!x || !raw || !y) return host_fail(M3G_EINVAL, "null argument");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return host_fail(M3G_ECUDA, "no CUDA device");
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;
+  return m3g::gemv_fused(dev, dtype, raw, raw_len, x, x2, gamma, res, xmode, y, static_cast<long long>(in_dim),
+                         static_cast<long long>(out_dim), st, false);
+}
+
+}  // extern "C"

@@ -8,6 +8,8 @@ namespace m3g {
 // Status bits the kernels set in the per-device error word.
 enum : uint32_t {
   kStatusCopyTimeout = 1u,  // a staged-copy wait gave up
+  kStatusBadPos = 2u,       // a decode step found its position outside the KV cache
+  kStatusBadToken = 4u,     // a decode step read a token id outside the vocabulary
 };
 
 // Arguments of the staged streaming GEMV (k_gemv_stream).
@@ -56,7 +58,29 @@ struct MmaArgs {
   int PRE;            // stages issued before the grid dependency resolves
   int rows_per_cta;
   int off_xsl, off_sum32, off_sum16, off_scale, off_red, off_bar;
+  // Fused input transform and epilogue (all zero for a plain GEMV):
+  //   xmode 0: the GEMV input is x
+  //   xmode 1: rms_norm(x) * gamma, the norm taken over all in_dim elements
+  //   xmode 2: silu(x) * x2 (the SwiGLU gate times the up projection)
+  //   res != nullptr: y[r] = res[r] + (W x')[r] (res may alias y)
+  const float* x2;
+  const float* gamma;  // nullptr: ones
+  const float* res;
+  int xmode;
 };
+
+enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
+
+// Fused GEMV on the tensor-core path only: M3G_OK, or an error code when the
+// shape has no tensor-core plan (the caller treats that as unsupported).
+// `coresident` sizes each CTA for half an SM so a following kernel's CTAs,
+// launched early by PDL, can start beside it.
+int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
+               const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
+               cudaStream_t st, bool coresident);
+
+// The per-device status word the kernels set kStatus* bits in.
+int status_word(int device, uint32_t** out);
 
 int mma_sb_bytes(int fmt);
 cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,

@@ -443,7 +443,8 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
           float acc = 0.f;
 #pragma unroll
           for (int w = 0; w < WK; ++w) acc += rb[lane * WK + w];
-          a.y[row0 + SR * grp + lane] = acc;
+          const long long r = row0 + SR * grp + lane;
+          a.y[r] = a.res ? a.res[r] + acc : acc;
         }
       }
       __syncwarp();
@@ -485,13 +486,51 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
   // every k-chunk), so it never waits for another warp; with two tiles per
   // stage the warp of tile 0 prepares and its tile-1 partner waits for it.
   if (ti == 0) {
+    // rms of x for the fused norm: every warp reduces all of x in the same
+    // order, so all warps of all CTAs agree on it without a barrier.
+    float rms = 1.f;
+    if (a.xmode == kXRmsNorm) {
+      const int n = 256 * a.NSB;
+      float ss = 0.f;
+      for (int i = 4 * lane; i < n; i += 128) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(a.x + i));
+        ss += q.x * q.x;
+        ss += q.y * q.y;
+        ss += q.z * q.z;
+        ss += q.w * q.w;
+      }
+      ss = warp_sum(ss);
+      rms = __fsqrt_rn(__fdiv_rn(ss, static_cast<float>(n)) + 1e-5f);
+    }
     for (int kcp = 0; kcp < a.NKC; ++kcp) {
       const int sb0p = kcp * a.KC;
       const int nsbp = min(a.KC, a.NSB - sb0p);
       for (int sb = sb0p + wk * nsbp / WK; sb < sb0p + (wk + 1) * nsbp / WK; ++sb) {
         const float4* xp4 = reinterpret_cast<const float4*>(a.x + 256 * sb + 8 * lane);
         const float4 v0 = __ldg(xp4), v1 = __ldg(xp4 + 1);
-        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        if (a.xmode == kXRmsNorm) {
+          // rms_norm_into: x / rms * gamma, each step rounded
+          float gm[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+          if (a.gamma) {
+            const float4* gp4 = reinterpret_cast<const float4*>(a.gamma + 256 * sb + 8 * lane);
+            const float4 g0 = __ldg(gp4), g1 = __ldg(gp4 + 1);
+            gm[0] = g0.x; gm[1] = g0.y; gm[2] = g0.z; gm[3] = g0.w;
+            gm[4] = g1.x; gm[5] = g1.y; gm[6] = g1.z; gm[7] = g1.w;
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdiv_rn(v[i], rms), gm[i]);
+        } else if (a.xmode == kXSiluMul) {
+          // g * sigmoid(g) * up, with sigmoid(g) = 1 / (1 + exp(-g))
+          const float4* up4 = reinterpret_cast<const float4*>(a.x2 + 256 * sb + 8 * lane);
+          const float4 u0 = __ldg(up4), u1 = __ldg(up4 + 1);
+          const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[i])));
+            v[i] = __fmul_rn(__fmul_rn(v[i], sg), u[i]);
+          }
+        }
         float amax = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));

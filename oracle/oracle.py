@@ -29,8 +29,8 @@ _sz = ctypes.c_size_t
 
 def build(force: bool = False) -> str:
     """Compile the oracle with its Makefile (gcc, strict IEEE flags)."""
-    src = os.path.join(_HERE, "m3q_oracle.c")
-    if force or not os.path.exists(_SO) or os.path.getmtime(_SO) < os.path.getmtime(src):
+    srcs = [os.path.join(_HERE, n) for n in ("m3q_oracle.c", "m3q_decode.c", "Makefile")]
+    if force or not os.path.exists(_SO) or any(os.path.getmtime(_SO) < os.path.getmtime(s) for s in srcs):
         subprocess.run(["make", "-s", "-C", _HERE], check=True)
     return _SO
 
@@ -244,3 +244,138 @@ def row_l1(raw, dtype: int, in_dim: int, out_dim: int) -> np.ndarray:
 def gemv_bound(raw, dtype: int, in_dim: int, out_dim: int, x) -> np.ndarray:
     """Per-row tolerance 1e-5 * ||row||_1 * ||x||_inf (the GEMV parity bound)."""
     return 1e-5 * row_l1(raw, dtype, in_dim, out_dim) * float(np.max(np.abs(np.asarray(x, np.float64))))
+
+
+# ---------------------------------------------------------------- decode step
+def _bind_decoder(L) -> None:
+    if getattr(L, "_decoder_bound", False):
+        return
+    vp = ctypes.c_void_p
+    L.or_decoder_create.argtypes = [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_int]
+    L.or_decoder_create.restype = vp
+    L.or_decoder_destroy.argtypes = [vp]
+    L.or_decoder_destroy.restype = None
+    L.or_decoder_set.argtypes = [vp, ctypes.c_int, vp, _sz, ctypes.c_uint32]
+    L.or_decoder_set.restype = ctypes.c_int
+    L.or_decoder_forward.argtypes = [vp, ctypes.c_uint32, _f32p, ctypes.c_int]
+    L.or_decoder_forward.restype = ctypes.c_int
+    L.or_decoder_pos.argtypes = [vp]
+    L.or_decoder_pos.restype = ctypes.c_int
+    L.or_decoder_reset.argtypes = [vp]
+    L.or_decoder_reset.restype = None
+    L.or_decoder_truncate.argtypes = [vp, ctypes.c_int]
+    L.or_decoder_truncate.restype = None
+    L.or_rms_norm_into.argtypes = [_f32p, _f32p, _f32p, _sz]
+    L.or_rms_norm_into.restype = None
+    L.or_rope_freqs.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_float, _f32p]
+    L.or_rope_freqs.restype = None
+    L.or_apply_rope.argtypes = [_f32p, _sz, ctypes.c_int, ctypes.c_int, _f32p]
+    L.or_apply_rope.restype = None
+    L.or_greedy.argtypes = [_f32p, _sz]
+    L.or_greedy.restype = ctypes.c_uint32
+    L.or_attention_head.argtypes = [_f32p, _f32p, _f32p, _sz, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
+    L.or_attention_head.restype = None
+    L._decoder_bound = True
+
+
+def rms_norm(x, gamma=None) -> np.ndarray:
+    """rms_norm_into (src/inference.rs:1575-1585)."""
+    L = lib()
+    _bind_decoder(L)
+    xa = _f32(x)
+    out = np.zeros_like(xa)
+    g = _f32(gamma) if gamma is not None else None
+    L.or_rms_norm_into(_p(xa, _f32p), _p(g, _f32p) if g is not None else None, _p(out, _f32p), xa.size)
+    return out
+
+
+def rope_freqs(pos: int, head_dim: int, theta: float) -> np.ndarray:
+    """(cos, sin) per pair for position `pos` (src/inference.rs:1000-1007), shape (head_dim/2, 2)."""
+    L = lib()
+    _bind_decoder(L)
+    cs = np.zeros((max(head_dim, 2) // 2, 2), np.float32)
+    L.or_rope_freqs(pos, head_dim, theta, _p(cs, _f32p))
+    return cs
+
+
+def apply_rope(v, n_heads: int, head_dim: int, cs) -> np.ndarray:
+    """apply_rope (src/inference.rs:1554-1572) on a copy of v."""
+    L = lib()
+    _bind_decoder(L)
+    out = _f32(v).copy()
+    c = _f32(cs)
+    L.or_apply_rope(_p(out, _f32p), out.size, n_heads, head_dim, _p(c, _f32p))
+    return out
+
+
+def greedy(logits) -> int:
+    """sample_with_params with top_k = 1 (src/inference.rs:1315-1369)."""
+    L = lib()
+    _bind_decoder(L)
+    la = _f32(logits)
+    return int(L.or_greedy(_p(la, _f32p), la.size))
+
+
+def attention_head(q, k_rows, v_rows) -> np.ndarray:
+    """One head over npos cached rows (src/inference.rs:1052-1079)."""
+    L = lib()
+    _bind_decoder(L)
+    qa, ka, va = _f32(q), _f32(k_rows), _f32(v_rows)
+    npos, hd = ka.shape
+    out = np.zeros(hd, np.float32)
+    scores = np.zeros(max(npos, 1), np.float32)
+    L.or_attention_head(_p(qa, _f32p), _p(ka, _f32p), _p(va, _f32p), hd, npos, hd, _p(out, _f32p), _p(scores, _f32p))
+    return out
+
+
+class Decoder:
+    """RealInference::forward_one on the CPU (src/inference.rs:953-1152).
+
+    ``tensors`` maps slot -> (uint8 or float32 array, ggml dtype); slots are
+    0 token_embd, 1 output_norm, 2 output, then 9 per layer (attn_norm, q, k,
+    v, o, ffn_norm, gate, up, down).  The arrays must outlive the decoder.
+    """
+
+    def __init__(self, n_layers, hidden, ffn, n_heads, n_kv_heads, vocab, rope_theta, max_pos, tensors,
+                 threads: int | None = None):
+        L = lib()
+        _bind_decoder(L)
+        self._L = L
+        self.vocab = vocab
+        self.threads = threads or default_threads()
+        self._h = L.or_decoder_create(n_layers, hidden, ffn, n_heads, n_kv_heads, vocab, rope_theta, max_pos)
+        if not self._h:
+            raise ValueError("bad decoder shape")
+        self._keep = []
+        for slot, (arr, dtype) in tensors.items():
+            a = np.ascontiguousarray(arr)
+            self._keep.append(a)
+            if not L.or_decoder_set(self._h, slot, a.ctypes.data, a.nbytes, dtype):
+                raise ValueError(f"bad slot {slot}")
+
+    def forward(self, token: int) -> np.ndarray:
+        logits = np.zeros(self.vocab, np.float32)
+        if not self._L.or_decoder_forward(self._h, token, _p(logits, _f32p), self.threads):
+            raise ValueError("forward_one failed (missing tensor, bad token or full cache)")
+        return logits
+
+    @property
+    def pos(self) -> int:
+        return int(self._L.or_decoder_pos(self._h))
+
+    def reset(self) -> None:
+        self._L.or_decoder_reset(self._h)
+
+    def truncate(self, n: int) -> None:
+        self._L.or_decoder_truncate(self._h, n)
+
+    def close(self) -> None:
+        if self._h:
+            self._L.or_decoder_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
