@@ -100,6 +100,13 @@ def load() -> ctypes.CDLL:
     global _lib
     if _lib is not None:
         return _lib
+    try:
+        # The library links libnccl.so.2 by soname.  Loading torch first makes
+        # both share torch's bundled NCCL; loading ours first would bind the
+        # system copy and break a later `import torch`.
+        import torch  # noqa: F401
+    except ImportError:
+        pass
     if not build_lib.up_to_date():
         try:
             build_lib.build()

@@ -87,6 +87,10 @@ struct Tuning {
   int64_t mma_cg = 4;           // rows per bulk copy when rows are contiguous (1 or 4)
   int64_t mma_pre = 1;          // stages prefetched before the previous kernel finishes
   int64_t mma_coresident = 0;   // size CTAs for half an SM so consecutive GEMVs overlap
+  int64_t decode_coresident = 1;  // the same for the GEMVs of a decode step
+  int64_t decode_pre = 1;         // mma_pre for the GEMVs of a decode step
+  int64_t mma_xfirst = 0;         // issue the ring past PRE only once x is loaded
+  int64_t decode_xfirst = 0;      // the same for the GEMVs of a decode step
 };
 Tuning g_tune;
 
@@ -291,6 +295,7 @@ int gemv_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const fl
     mp.a.x = x;
     mp.a.y = y;
     mp.a.status = ds.status;
+    mp.a.xfirst = static_cast<int>(g_tune.mma_xfirst);
     cudaError_t e = m3g::launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);
     if (e != cudaSuccess) return cuda_fail(e, "k_gemv_mma launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -385,7 +390,8 @@ bool block_geometry(uint32_t dtype, int* be, int* bb) {
 
 int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
-               cudaStream_t st, bool coresident) {
+               cudaStream_t st, bool decode, unsigned long long* argmax_key) {
+  const bool coresident = decode && g_tune.decode_coresident;
   FmtInfo f;
   if (int rc = gemv_rules(dtype, raw_len, static_cast<uint64_t>(in_dim), static_cast<uint64_t>(out_dim), f)) return rc;
   if (xmode < kXPlain || xmode > kXSiluMul) return fail(M3G_EINVAL, "unknown input transform %d", xmode);
@@ -410,6 +416,9 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
   mp.a.gamma = gamma;
   mp.a.res = res;
   mp.a.xmode = xmode;
+  mp.a.argmax_key = argmax_key;
+  mp.a.xfirst = static_cast<int>(decode ? g_tune.decode_xfirst : g_tune.mma_xfirst);
+  if (decode) mp.a.PRE = static_cast<int>(g_tune.decode_pre);
   cudaError_t e = launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);
   if (e != cudaSuccess) return cuda_fail(e, "k_gemv_mma launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -459,6 +468,10 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "mma_cg") && (value == 1 || value == 4)) g_tune.mma_cg = value;
   else if (!strcmp(key, "mma_pre") && value >= 0 && value <= 8) g_tune.mma_pre = value;
   else if (!strcmp(key, "mma_coresident")) g_tune.mma_coresident = value != 0;
+  else if (!strcmp(key, "decode_coresident")) g_tune.decode_coresident = value != 0;
+  else if (!strcmp(key, "decode_pre") && value >= 0 && value <= 8) g_tune.decode_pre = value;
+  else if (!strcmp(key, "mma_xfirst")) g_tune.mma_xfirst = value != 0;
+  else if (!strcmp(key, "decode_xfirst")) g_tune.decode_xfirst = value != 0;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }

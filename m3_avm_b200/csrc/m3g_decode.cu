@@ -15,7 +15,9 @@
 //     GEMV  gate|up   rms_norm(hidden) * ffn_norm input, gate|up rows concatenated
 //     GEMV  down      silu(gate) * up input, hidden += W_down (...)
 //   GEMV  head        rms_norm(hidden) * output_norm -> logits
-//   k_argmax_step     greedy token (lowest index of the largest logit) into
+//                     whose epilogue also reduces (logit, row) to the greedy
+//                     pick with one 64-bit atomicMax per CTA
+//   k_pick_step       the pick (lowest index of the largest logit) into
 //                     tokens[pos + 1] unless that slot holds a given prompt
 //                     token, then pos += 1
 //
@@ -215,46 +217,20 @@ __global__ void __launch_bounds__(256) k_embed(const uint8_t* __restrict__ w, in
 }
 
 // Greedy pick (sample_with_params with top_k = 1: the first index holding
-// the largest logit) and the step's bookkeeping.
-__global__ void __launch_bounds__(1024) k_argmax_step(const float* __restrict__ logits, int n, int* pos, int* tokens,
-                                                      const int* nfixed, int max_pos, int* last) {
-  __shared__ float bvs[32];
-  __shared__ int bis[32];
+// the largest logit) from the key the head GEMV's epilogue reduced with
+// atomicMax, and the step's bookkeeping; the key is cleared for the next step.
+__global__ void __launch_bounds__(32) k_pick_step(unsigned long long* key, int* pos, int* tokens, const int* nfixed,
+                                                  int max_pos, int* last) {
   grid_dep_wait();
   grid_dep_launch();
-  float bv = -INFINITY;
-  int bi = 0x7FFFFFFF;
-  const int n4 = n / 4;
-  for (int i4 = threadIdx.x; i4 < n4; i4 += 1024) {
-    const float4 v = reinterpret_cast<const float4*>(logits)[i4];
-    const int i = 4 * i4;
-    if (v.x > bv) { bv = v.x; bi = i; }
-    if (v.y > bv) { bv = v.y; bi = i + 1; }
-    if (v.z > bv) { bv = v.z; bi = i + 2; }
-    if (v.w > bv) { bv = v.w; bi = i + 3; }
-  }
-  for (int i = 4 * n4 + threadIdx.x; i < n; i += 1024) {
-    const float v = logits[i];
-    if (v > bv) { bv = v; bi = i; }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-    const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-  }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) { bvs[warp] = bv; bis[warp] = bi; }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < 32; ++w)
-      if (bvs[w] > bv || (bvs[w] == bv && bis[w] < bi)) { bv = bvs[w]; bi = bis[w]; }
-    if (bi == 0x7FFFFFFF) bi = 0;  // every logit NaN
-    const int p = *pos, next = p + 1;
-    *last = bi;
-    if (next <= max_pos && next >= *nfixed) tokens[next] = bi;
-    *pos = next;
-  }
+  if (threadIdx.x != 0) return;
+  const unsigned long long k = *key;
+  const int pick = k ? static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k)) : 0;  // 0: every logit NaN
+  const int p = *pos, next = p + 1;
+  *last = pick;
+  if (next <= max_pos && next >= *nfixed) tokens[next] = pick;
+  *pos = next;
+  *key = 0ull;
 }
 
 template <class Kern, class... Args>
@@ -322,6 +298,7 @@ struct m3g_decoder {
   float *hidden = nullptr, *qkvb = nullptr, *att = nullptr, *gub = nullptr, *logits = nullptr;
   float *rope = nullptr, *kc = nullptr, *vc = nullptr;
   int *dpos = nullptr, *tokens = nullptr, *nfixed = nullptr, *last = nullptr;
+  unsigned long long* key = nullptr;  // greedy pick of the step (argmax epilogue of the head GEMV)
   int* h_io = nullptr;  // pinned: [0] token / nfixed staging, [1] last token
   uint32_t* status = nullptr;
   int pos = 0;           // host mirror of the device position
@@ -408,8 +385,8 @@ int prepare(m3g_decoder* d) {
 }
 
 int gemv(m3g_decoder* d, const Gemv& g, const float* x, const float* x2, const float* gamma, const float* res,
-         int xmode, float* y) {
-  return m3g::gemv_fused(d->device, g.dtype, g.w, g.len, x, x2, gamma, res, xmode, y, g.in, g.out, d->st, true);
+         int xmode, float* y, unsigned long long* key = nullptr) {
+  return m3g::gemv_fused(d->device, g.dtype, g.w, g.len, x, x2, gamma, res, xmode, y, g.in, g.out, d->st, true, key);
 }
 
 // Enqueue one decode step on d->st (also the body the graph captures).
@@ -467,9 +444,10 @@ int enqueue_step(m3g_decoder* d) {
       return rc;
   }
   const float* g_out = reinterpret_cast<const float*>(d->t[kSlotOutNorm].d);
-  if (int rc = gemv(d, part(d->t[kSlotOut]), d->hidden, nullptr, g_out, nullptr, m3g::kXRmsNorm, d->logits)) return rc;
-  DEC_CUDA(m3g::launch_pdl(m3g::k_argmax_step, dim3(1), dim3(1024), 0, d->st, static_cast<const float*>(d->logits), V,
-                           d->dpos, d->tokens, static_cast<const int*>(d->nfixed), mp, d->last));
+  if (int rc = gemv(d, part(d->t[kSlotOut]), d->hidden, nullptr, g_out, nullptr, m3g::kXRmsNorm, d->logits, d->key))
+    return rc;
+  DEC_CUDA(m3g::launch_pdl(m3g::k_pick_step, dim3(1), dim3(32), 0, d->st, d->key, d->dpos, d->tokens,
+                           static_cast<const int*>(d->nfixed), mp, d->last));
   return M3G_OK;
 }
 
@@ -585,6 +563,7 @@ M3G_API int m3g_decoder_create(int device, const m3g_decoder_config* cfg, m3g_de
   if (e == cudaSuccess) e = cudaMalloc(&d->kc, 4 * c.n_layers * mp * d->kvd);
   if (e == cudaSuccess) e = cudaMalloc(&d->vc, 4 * c.n_layers * mp * d->kvd);
   if (e == cudaSuccess) e = cudaMalloc(&d->dpos, 4 * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&d->key, 16);
   if (e == cudaSuccess) e = cudaMalloc(&d->tokens, 4 * (mp + 1));
   if (e == cudaSuccess) e = cudaHostAlloc(&d->h_io, 4 * 4, cudaHostAllocDefault);
   if (e != cudaSuccess) {
@@ -605,6 +584,7 @@ M3G_API int m3g_decoder_create(int device, const m3g_decoder_config* cfg, m3g_de
     }
   e = cudaMemcpy(d->rope, rope.data(), 4 * mp * hd, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(d->dpos, 0, 4 * 4);
+  if (e == cudaSuccess) e = cudaMemset(d->key, 0, 16);
   if (e == cudaSuccess) e = cudaMemset(d->tokens, 0, 4 * (mp + 1));
   if (e == cudaSuccess) {
     const size_t attn_smem = sizeof(float) * (3 * hd + m3g::kAttnWarps * hd + 64 + mp);
@@ -730,6 +710,7 @@ M3G_API int m3g_decoder_truncate(m3g_decoder* d, uint64_t n) {
   DEC_CUDA(cudaStreamSynchronize(d->st));
   const int p = static_cast<int>(n);
   DEC_CUDA(cudaMemcpy(d->dpos, &p, 4, cudaMemcpyHostToDevice));
+  DEC_CUDA(cudaMemset(d->key, 0, 16));
   d->pos = p;
   d->pending = false;
   return M3G_OK;
@@ -759,7 +740,7 @@ M3G_API void m3g_decoder_destroy(m3g_decoder* d) {
   for (void* p : {static_cast<void*>(d->hidden), static_cast<void*>(d->qkvb), static_cast<void*>(d->att),
                   static_cast<void*>(d->gub), static_cast<void*>(d->logits), static_cast<void*>(d->rope),
                   static_cast<void*>(d->kc), static_cast<void*>(d->vc), static_cast<void*>(d->dpos),
-                  static_cast<void*>(d->tokens)})
+                  static_cast<void*>(d->tokens), static_cast<void*>(d->key)})
     if (p) cudaFree(p);
   if (d->h_io) cudaFreeHost(d->h_io);
   if (d->st) cudaStreamDestroy(d->st);

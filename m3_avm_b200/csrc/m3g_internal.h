@@ -67,17 +67,24 @@ struct MmaArgs {
   const float* gamma;  // nullptr: ones
   const float* res;
   int xmode;
+  // Non-null: atomicMax of argmax_key(y[r], r) over the rows (the greedy
+  // pick, decoded as 0xFFFFFFFF - low word; the caller zeroes it first).
+  unsigned long long* argmax_key;
+  // 1: stages past the first PRE are issued only after the consumers have
+  // loaded x (their loads then do not wait behind the weight stream).
+  int xfirst;
 };
 
 enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
 
 // Fused GEMV on the tensor-core path only: M3G_OK, or an error code when the
 // shape has no tensor-core plan (the caller treats that as unsupported).
-// `coresident` sizes each CTA for half an SM so a following kernel's CTAs,
-// launched early by PDL, can start beside it.
+// `decode` plans for a chain of small GEMVs: CTAs sized for half an SM (when
+// the rows allow) so the next kernel's CTAs, launched early by PDL, start
+// streaming their weights beside the running one.
 int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
-               cudaStream_t st, bool coresident);
+               cudaStream_t st, bool decode, unsigned long long* argmax_key = nullptr);
 
 // The per-device status word the kernels set kStatus* bits in.
 int status_word(int device, uint32_t** out);

@@ -361,10 +361,68 @@ struct MmaQ40 {
   }
 };
 
+// (value, row) packed so that unsigned order is the greedy order: larger value
+// first, then the lower row (the first index of the maximum).  The value maps
+// to an order-preserving unsigned word; key 0 is below every finite value.
+__device__ __forceinline__ unsigned long long argmax_key(float v, long long row) {
+  const uint32_t u = v == 0.f ? 0u : __float_as_uint(v);  // -0 ties with +0
+  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(row));
+}
+
+// x -> three int8 slices of super-block sb and its group sums; lane holds
+// elements 8*lane .. 8*lane+7 in v.
+__device__ __forceinline__ void quantize_sb(const float (&v)[8], int sb, int lane, uint8_t* xsl, float* sum32,
+                                            float* sum16, float* sxs) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+  uint32_t s0[2] = {0u, 0u}, s1[2] = {0u, 0u}, s2[2] = {0u, 0u};
+  float part = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    part += v[i];
+    const float q = v[i] * inv;
+    const float q0 = rintf(q);
+    const float u1 = (q - q0) * 254.0f;
+    const float q1 = rintf(u1);
+    const float q2 = rintf((u1 - q1) * 254.0f);
+    const int sh = 8 * (i & 3);
+    s0[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q0)) & 0xFFu) << sh;
+    s1[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q1)) & 0xFFu) << sh;
+    s2[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q2)) & 0xFFu) << sh;
+  }
+  // lane covers elements 8*lane .. +8: sub-block j = lane / 4, offset 8 * (lane % 4)
+  uint8_t* dst = xsl + (static_cast<size_t>(sb) * 8 + (lane >> 2)) * 96 + 8 * (lane & 3);
+  *reinterpret_cast<uint2*>(dst) = make_uint2(s0[0], s0[1]);
+  *reinterpret_cast<uint2*>(dst + 32) = make_uint2(s1[0], s1[1]);
+  *reinterpret_cast<uint2*>(dst + 64) = make_uint2(s2[0], s2[1]);
+  const float p16 = part + __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+  if ((lane & 1) == 0) sum16[sb * 16 + (lane >> 1)] = p16;
+  const float p32 = p16 + __shfl_xor_sync(0xFFFFFFFFu, p16, 2);
+  if ((lane & 3) == 0) sum32[sb * 8 + (lane >> 2)] = p32;
+  if (lane == 0) sxs[sb] = amax > 0.f ? amax / 127.0f : 0.f;
+}
+
+// Named barriers of the kernel (0 is __syncthreads): 1..WK pair the warps of
+// two-tile stages (TPS > 1); the next id combines the norm's partial sums and
+// the one after releases the producer once x is loaded.  Ids stay low: the
+// highest id used sets the barriers a CTA reserves.
+template <int TPS, int WK>
+struct Bars {
+  static constexpr int kRms = TPS > 1 ? WK + 1 : 1;
+  static constexpr int kXLoaded = kRms + 1;
+};
+
 // ---------------------------------------------------------------- the kernel
 // TPS 16-row tiles per stage; WK consumer warps per tile split its k-chunk of
 // at most 16 super-blocks, so a warp owns at most 16 / WK of them.
-template <class F, int TPS, int WK>
+// FUSED adds the decode-step features (input transforms, residual and argmax
+// epilogues, x-first issue); the plain GEMV is compiled without them.
+template <class F, int TPS, int WK, bool FUSED>
 __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaArgs a) {
   constexpr int NCW = WK * TPS;  // consumer warps
   constexpr int SR = 16 * TPS;   // rows per stage
@@ -428,10 +486,17 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
     for (int s = 0; s < pre; ++s) issue(s);
     grid_dep_wait();
     grid_dep_launch();
+    // x first: with XFIRST the rest of the ring waits until the preparing
+    // warps hold x in registers, so their L2 reads do not queue behind a
+    // burst of weight misses.
+    if constexpr (FUSED) {
+      if (a.xfirst) named_bar_sync(Bars<TPS, WK>::kXLoaded, 32 * (WK + 1));
+    }
     for (int s = pre; s < min(a.NS, nst); ++s) issue(s);
     int buf = 0;
     uint32_t ph = 0;
     bool ok = true;
+    unsigned long long best_key = 0ull;  // argmax epilogue: this lane's best (value, row)
     for (int s = 0; s < nst; ++s) {
       ok = mbar_wait_bounded(&empty[buf], ph, kMmaTimeoutNs, abort_flag);
       if (!ok) break;
@@ -444,7 +509,13 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
 #pragma unroll
           for (int w = 0; w < WK; ++w) acc += rb[lane * WK + w];
           const long long r = row0 + SR * grp + lane;
-          a.y[r] = a.res ? a.res[r] + acc : acc;
+          if constexpr (FUSED) {
+            const float yv = a.res ? a.res[r] + acc : acc;
+            a.y[r] = yv;
+            if (a.argmax_key && yv == yv) best_key = max(best_key, argmax_key(yv, r));
+          } else {
+            a.y[r] = acc;
+          }
         }
       }
       __syncwarp();
@@ -453,6 +524,13 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
         issue(s + a.NS);
       }
       if (++buf == a.NS) { buf = 0; ph ^= 1u; }
+    }
+    if constexpr (FUSED) {
+      if (a.argmax_key) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) best_key = max(best_key, __shfl_xor_sync(0xFFFFFFFFu, best_key, o));
+        if (lane == 0 && best_key) atomicMax(a.argmax_key, best_key);
+      }
     }
     if (!ok && lane == 0) {
       *abort_flag = 1;
@@ -480,89 +558,128 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
   float* sum32 = reinterpret_cast<float*>(smem + a.off_sum32);
   float* sum16 = reinterpret_cast<float*>(smem + a.off_sum16);
   float* sxs = reinterpret_cast<float*>(smem + a.off_scale);
-  grid_dep_wait();
   // x -> per-super-block int8 slices and group sums (lane: 8 elements).  Each
   // warp prepares exactly the super-blocks it consumes (its share [j0, j1) of
   // every k-chunk), so it never waits for another warp; with two tiles per
   // stage the warp of tile 0 prepares and its tile-1 partner waits for it.
-  if (ti == 0) {
-    // rms of x for the fused norm: every warp reduces all of x in the same
-    // order, so all warps of all CTAs agree on it without a barrier.
-    float rms = 1.f;
-    if (a.xmode == kXRmsNorm) {
-      const int n = 256 * a.NSB;
-      float ss = 0.f;
-      for (int i = 4 * lane; i < n; i += 128) {
-        const float4 q = __ldg(reinterpret_cast<const float4*>(a.x + i));
-        ss += q.x * q.x;
-        ss += q.y * q.y;
-        ss += q.z * q.z;
-        ss += q.w * q.w;
-      }
-      ss = warp_sum(ss);
-      rms = __fsqrt_rn(__fdiv_rn(ss, static_cast<float>(n)) + 1e-5f);
-    }
-    for (int kcp = 0; kcp < a.NKC; ++kcp) {
-      const int sb0p = kcp * a.KC;
-      const int nsbp = min(a.KC, a.NSB - sb0p);
-      for (int sb = sb0p + wk * nsbp / WK; sb < sb0p + (wk + 1) * nsbp / WK; ++sb) {
-        const float4* xp4 = reinterpret_cast<const float4*>(a.x + 256 * sb + 8 * lane);
-        const float4 v0 = __ldg(xp4), v1 = __ldg(xp4 + 1);
-        float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        if (a.xmode == kXRmsNorm) {
-          // rms_norm_into: x / rms * gamma, each step rounded
-          float gm[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
-          if (a.gamma) {
-            const float4* gp4 = reinterpret_cast<const float4*>(a.gamma + 256 * sb + 8 * lane);
-            const float4 g0 = __ldg(gp4), g1 = __ldg(gp4 + 1);
-            gm[0] = g0.x; gm[1] = g0.y; gm[2] = g0.z; gm[3] = g0.w;
-            gm[4] = g1.x; gm[5] = g1.y; gm[6] = g1.z; gm[7] = g1.w;
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdiv_rn(v[i], rms), gm[i]);
-        } else if (a.xmode == kXSiluMul) {
-          // g * sigmoid(g) * up, with sigmoid(g) = 1 / (1 + exp(-g))
-          const float4* up4 = reinterpret_cast<const float4*>(a.x2 + 256 * sb + 8 * lane);
-          const float4 u0 = __ldg(up4), u1 = __ldg(up4 + 1);
-          const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[i])));
-            v[i] = __fmul_rn(__fmul_rn(v[i], sg), u[i]);
-          }
+  if constexpr (!FUSED) {
+    grid_dep_wait();
+    // x -> per-super-block int8 slices and group sums (lane: 8 elements).  Each
+    // warp prepares exactly the super-blocks it consumes (its share [j0, j1) of
+    // every k-chunk), so it never waits for another warp; with two tiles per
+    // stage the warp of tile 0 prepares and its tile-1 partner waits for it.
+    if (ti == 0) {
+      for (int kcp = 0; kcp < a.NKC; ++kcp) {
+        const int sb0p = kcp * a.KC;
+        const int nsbp = min(a.KC, a.NSB - sb0p);
+        for (int sb = sb0p + wk * nsbp / WK; sb < sb0p + (wk + 1) * nsbp / WK; ++sb) {
+          const float4* xp4 = reinterpret_cast<const float4*>(a.x + 256 * sb + 8 * lane);
+          const float4 v0 = __ldg(xp4), v1 = __ldg(xp4 + 1);
+          const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+          quantize_sb(v, sb, lane, xsl, sum32, sum16, sxs);
         }
-        float amax = 0.f;
+      }
+    }
+  } else {
+    if (ti == 0) {
+      // This warp's super-blocks: its share [wk*n/WK, (wk+1)*n/WK) of every
+      // k-chunk, visited in order; sb < 0 ends the walk.
+      auto first_sb = [&](int kcp) -> int {
+        for (; kcp < a.NKC; ++kcp) {
+          const int sb0p = kcp * a.KC, nsbp = min(a.KC, a.NSB - sb0p);
+          if (wk * nsbp / WK < (wk + 1) * nsbp / WK) return sb0p + wk * nsbp / WK;
+        }
+        return -1;
+      };
+      auto next_sb = [&](int sb) -> int {
+        const int kcp = sb / a.KC, sb0p = kcp * a.KC, nsbp = min(a.KC, a.NSB - sb0p);
+        return sb + 1 < sb0p + (wk + 1) * nsbp / WK ? sb + 1 : first_sb(kcp + 1);
+      };
+      auto load8 = [&](const float* base, int sb, float (&v)[8]) {
+        const float4* p4 = reinterpret_cast<const float4*>(base + 256 * sb + 8 * lane);
+        const float4 v0 = __ldg(p4), v1 = __ldg(p4 + 1);
+        v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
+        v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
+      };
+      // Transform (fused norm or SwiGLU), quantise into three int8 slices and
+      // store the slices and group sums of super-block sb.
+      auto prep = [&](int sb, float (&v)[8], const float (&gm)[8], const float (&u)[8], float inv_rms) {
+        if (a.xmode == kXRmsNorm) {
+          // rms_norm_into, x / rms * gamma, as x * (1 / rms) * gamma: within an
+          // ulp of the reference per element
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+          for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], inv_rms), gm[i]);
+        } else if (a.xmode == kXSiluMul) {
+          // g * sigmoid(g) * up = g * up / (1 + exp(-g)), fast exponential and
+          // division (relative error ~|g| * 2^-22); a huge 1 + exp(-g) divides
+          // to 0, the limit of the sigmoid.
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-        const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-        uint32_t s0[2] = {0u, 0u}, s1[2] = {0u, 0u}, s2[2] = {0u, 0u};
-        float part = 0.f;
+          for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdividef(v[i], 1.0f + __expf(-v[i])), u[i]);
+        }
+        quantize_sb(v, sb, lane, xsl, sum32, sum16, sxs);
+      };
+      // The first two super-blocks of this warp stay in registers, so all of
+      // their loads are in flight together: the norm weights (constant) before
+      // the grid dependency resolves, x (and the up projection) right after.
+      const int sbA = first_sb(0);
+      const int sbB = sbA >= 0 ? next_sb(sbA) : -1;
+      const int sbC = sbB >= 0 ? next_sb(sbB) : -1;  // further ones: one at a time
+      float gA[8], gB[8], xA[8], xB[8], uA[8], uB[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gA[i] = gB[i] = uA[i] = uB[i] = 1.f;
+      if (a.xmode == kXRmsNorm && a.gamma) {
+        if (sbA >= 0) load8(a.gamma, sbA, gA);
+        if (sbB >= 0) load8(a.gamma, sbB, gB);
+      }
+      grid_dep_wait();
+      grid_dep_launch();
+      if (sbA >= 0) load8(a.x, sbA, xA);
+      if (sbB >= 0) load8(a.x, sbB, xB);
+      if (a.xmode == kXSiluMul) {
+        if (sbA >= 0) load8(a.x2, sbA, uA);
+        if (sbB >= 0) load8(a.x2, sbB, uB);
+      }
+      float inv_rms = 1.f;
+      if (a.xmode == kXRmsNorm) {
+        // Sum of squares: each warp over its own super-blocks, then the WK
+        // preparing warps combine their partials in a fixed order through
+        // shared memory, so every CTA derives the same rms.
+        float ss = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          part += v[i];
-          const float u = v[i] * inv;
-          const float q0 = rintf(u);
-          const float u1 = (u - q0) * 254.0f;
-          const float q1 = rintf(u1);
-          const float q2 = rintf((u1 - q1) * 254.0f);
-          const int sh = 8 * (i & 3);
-          s0[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q0)) & 0xFFu) << sh;
-          s1[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q1)) & 0xFFu) << sh;
-          s2[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q2)) & 0xFFu) << sh;
+          if (sbA >= 0) ss = fmaf(xA[i], xA[i], ss);
+          if (sbB >= 0) ss = fmaf(xB[i], xB[i], ss);
         }
-        // lane covers elements 8*lane .. +8: sub-block j = lane / 4, offset 8 * (lane % 4)
-        uint8_t* dst = xsl + (static_cast<size_t>(sb) * 8 + (lane >> 2)) * 96 + 8 * (lane & 3);
-        *reinterpret_cast<uint2*>(dst) = make_uint2(s0[0], s0[1]);
-        *reinterpret_cast<uint2*>(dst + 32) = make_uint2(s1[0], s1[1]);
-        *reinterpret_cast<uint2*>(dst + 64) = make_uint2(s2[0], s2[1]);
-        const float p16 = part + __shfl_xor_sync(0xFFFFFFFFu, part, 1);
-        if ((lane & 1) == 0) sum16[sb * 16 + (lane >> 1)] = p16;
-        const float p32 = p16 + __shfl_xor_sync(0xFFFFFFFFu, p16, 2);
-        if ((lane & 3) == 0) sum32[sb * 8 + (lane >> 2)] = p32;
-        if (lane == 0) sxs[sb] = amax > 0.f ? amax / 127.0f : 0.f;
+        for (int sb = sbC; sb >= 0; sb = next_sb(sb)) {
+          float v[8];
+          load8(a.x, sb, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+        }
+        ss = warp_sum(ss);
+        float* part = reinterpret_cast<float*>(smem + a.off_red);  // free until the first tile ends
+        if (lane == 0) part[wk] = ss;
+        named_bar_sync(Bars<TPS, WK>::kRms, 32 * WK);
+        float tot = 0.f;
+        for (int w = 0; w < WK; ++w) tot += part[w];
+        named_bar_sync(Bars<TPS, WK>::kRms, 32 * WK);
+        inv_rms = __frcp_rn(__fsqrt_rn(__fdiv_rn(tot, static_cast<float>(256 * a.NSB)) + 1e-5f));
       }
+      if (sbA >= 0) prep(sbA, xA, gA, uA, inv_rms);
+      if (sbB >= 0) prep(sbB, xB, gB, uB, inv_rms);
+      if (a.xfirst) named_bar_arrive(Bars<TPS, WK>::kXLoaded, 32 * (WK + 1));  // x, x2 of sbA, sbB are consumed
+      for (int sb = sbC; sb >= 0; sb = next_sb(sb)) {
+        float v[8], gm[8], u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) gm[i] = u[i] = 1.f;
+        load8(a.x, sb, v);
+        if (a.xmode == kXRmsNorm && a.gamma) load8(a.gamma, sb, gm);
+        if (a.xmode == kXSiluMul) load8(a.x2, sb, u);
+        prep(sb, v, gm, u, inv_rms);
+      }
+    } else {
+      grid_dep_wait();
+      grid_dep_launch();
     }
   }
   if (TPS > 1) named_bar_sync(1 + wk, 64);  // warps wk (tile 0) and WK + wk (tile 1)
@@ -662,12 +779,20 @@ int mma_sb_bytes(int fmt) {
   }
 }
 
+template <class F, bool FUSED>
+static cudaError_t launch_mma_cfg(const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
+                                  bool pdl) {
+  if (wk == 16) return launch_mma_kernel<k_gemv_mma<F, 1, 16, FUSED>>(a, grid, 32 * 17, smem, st, pdl);
+  if (tps == 2) return launch_mma_kernel<k_gemv_mma<F, 2, 8, FUSED>>(a, grid, 32 * 17, smem, st, pdl);
+  return launch_mma_kernel<k_gemv_mma<F, 1, 8, FUSED>>(a, grid, 32 * 9, smem, st, pdl);
+}
+
 template <class F>
 static cudaError_t launch_mma_fmt(const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
                                   bool pdl) {
-  if (wk == 16) return launch_mma_kernel<k_gemv_mma<F, 1, 16>>(a, grid, 32 * 17, smem, st, pdl);
-  if (tps == 2) return launch_mma_kernel<k_gemv_mma<F, 2, 8>>(a, grid, 32 * 17, smem, st, pdl);
-  return launch_mma_kernel<k_gemv_mma<F, 1, 8>>(a, grid, 32 * 9, smem, st, pdl);
+  const bool fused = a.xmode != kXPlain || a.res || a.argmax_key || a.xfirst;
+  return fused ? launch_mma_cfg<F, true>(a, tps, wk, grid, smem, st, pdl)
+               : launch_mma_cfg<F, false>(a, tps, wk, grid, smem, st, pdl);
 }
 
 cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
