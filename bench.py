@@ -14,6 +14,11 @@ bytes (weights + x + y) with inputs resident; `e2e` is the same metric through
 the GpuOffload-shaped C ABI call with host x and y (copies in the timed
 region).  Under torchrun every rank runs its own GEMV stream (weak scaling, no
 data-path collective); the time is the max over ranks.
+
+The second half of the metric, decode tokens/s, is the `decode` object of the
+same line: greedy decode of a Llama-3.2-1B-shaped model (Q4_K_M mix) through
+the device-resident engine, 128 prompt tokens then 256 generated, with the
+C restatement of the reference's CPU forward pass timed beside it.
 """
 from __future__ import annotations
 
@@ -34,7 +39,7 @@ sys.path.insert(0, ROOT)
 
 IN_DIM, OUT_DIM, DTYPE = 4096, 14336, 12
 WORKLOAD = "q4k_gemv_14336x4096"
-METRIC = "Q4_K GEMV HBM GB/s (% of peak) @4096x14336"
+METRIC = "Q4_K GEMV HBM GB/s (% of peak) @4096x14336; 1B decode tokens/sec"
 
 
 def algorithmic_bytes(in_dim: int, out_dim: int, dtype: int, batch: int = 1) -> int:
@@ -145,6 +150,96 @@ def cpu_gemv_rate(threads: int, target_s: float, max_calls: int | None = None) -
             "median_s": med}
 
 
+DECODE_PROMPT, DECODE_GEN = 128, 256
+
+
+def decode_leg(args, dev) -> dict:
+    """Greedy decode of the Llama-3.2-1B-shaped model (16 layers, hidden 2048,
+    FFN 8192, 32/8 heads x 64, vocab 128256, Q4_K attention/gate/up/embedding,
+    Q6_K down and head), seeded synthetic weights: a 128-token prompt, then
+    256 generated tokens, all steps device-resident."""
+    import torch
+
+    from m3_avm_b200 import model
+    from m3_avm_b200.decoder import GpuDecoder
+
+    shape = model.LLAMA_1B
+    tensors = model.synthetic_tensors(shape, seed=1)
+    prompt = model.prompt_tokens(shape, DECODE_PROMPT, seed=2)
+    dec = GpuDecoder(shape, max_pos=DECODE_PROMPT + DECODE_GEN + 8, device=dev.index or 0)
+    dec.upload_all(tensors)
+    dec.set_graph(not args.no_graph)
+    st = torch.cuda.ExternalStream(dec.stream, device=dev)
+    # warm-up: one full prompt + a few steps (graph capture, lazy setup)
+    dec.prefill_logits(prompt)
+    dec.run_async(8)
+    dec.sync()
+    dec.clear_kv_cache()
+    dec.prefill_logits(prompt)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    dec.run_async(DECODE_GEN - 1)  # the first generated token is the prefill's pick
+    e1.record(st)
+    dec.sync()
+    gen_ms = e0.elapsed_time(e1)
+    toks = dec.tokens(DECODE_PROMPT, DECODE_GEN)
+    tok_s = (DECODE_GEN - 1) / (gen_ms / 1e3)
+    # e2e: the public call a user makes, host prompt in, host tokens out
+    dec.clear_kv_cache()
+    t0 = time.perf_counter()
+    toks2 = dec.generate(prompt, DECODE_GEN)
+    e2e_s = time.perf_counter() - t0
+    dec.close()
+    bytes_tok = shape.weight_bytes_per_token()
+    peaks, kind = measured_peaks()
+    peak = float(peaks["hbm_gbs"])
+    out = {
+        "workload": "llama-3.2-1b-shaped greedy decode, Q4_K_M mix (Q4_K attn/gate/up/embd, Q6_K down/head)",
+        "prompt_tokens": DECODE_PROMPT, "generated_tokens": DECODE_GEN,
+        "tokens_per_s": round(tok_s, 1), "us_per_token": round(gen_ms * 1e3 / (DECODE_GEN - 1), 2),
+        "timing": "CUDA events on the decoder stream around the 255 generation steps after the prompt",
+        "roofline": {"bound": "hbm", "weight_bytes_per_token": bytes_tok,
+                     "achieved_gbs": round(bytes_tok * tok_s / 1e9, 1), "peak": peak, "peak_kind": kind,
+                     "frac": round(bytes_tok * tok_s / 1e9 / peak, 4),
+                     "roofline_tokens_per_s": round(peak * 1e9 / bytes_tok, 1)},
+        "e2e": {"value": round(DECODE_GEN / e2e_s, 1), "unit": "tokens/s",
+                "api": "m3g_decoder_prefill + m3g_decoder_generate (host prompt in, host tokens out; "
+                       "includes the 128-token prefill)",
+                "h2d_bytes_per_step": 4 * DECODE_PROMPT, "d2h_bytes_per_step": 4 * DECODE_GEN,
+                "seconds": round(e2e_s, 4)},
+        "tokens_match_e2e": bool((toks == toks2).all()),
+        "graph": not args.no_graph,
+        "gpu_launches_per_token": 1 + 5 * shape.n_layers + 2,
+    }
+    if not args.no_cpu:
+        out["cpu_baseline"] = cpu_decode_rate(shape, tensors, prompt)
+    return out
+
+
+def cpu_decode_rate(shape, tensors, prompt, n_tokens: int = 3) -> dict:
+    """The oracle's restatement of forward_one (reference CPU path) on the host cores."""
+    from oracle import oracle as O
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    dec = O.Decoder(shape.n_layers, shape.hidden, shape.ffn, shape.n_heads, shape.n_kv_heads, shape.vocab,
+                    shape.rope_theta, 64, tensors, threads=threads)
+    t0 = time.perf_counter()
+    dec.forward(int(prompt[0]))  # dequantises and caches the f32 head, like the reference's first token
+    first = time.perf_counter() - t0
+    times = []
+    for t in prompt[1:1 + n_tokens]:
+        t0 = time.perf_counter()
+        dec.forward(int(t))
+        times.append(time.perf_counter() - t0)
+    dec.close()
+    med = statistics.median(times)
+    return {"value": round(1.0 / med, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n_tokens} forward_one steps after a first step of {first:.2f} s (C restatement of "
+                      f"RealInference::forward_one with matvec_quant and the f32-cached head, {threads} OpenMP "
+                      f"threads), median {med * 1e3:.1f} ms"}
+
+
 def run_reference(args) -> int:
     rank, world, _ = dist_env()
     if rank != 0:
@@ -183,6 +278,13 @@ def run_reference(args) -> int:
                                    f"reference AVX2 matvec_q4k; the Rust crate cannot be built here)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_decode:
+        from m3_avm_b200 import model
+
+        shape = model.LLAMA_1B
+        line["decode"] = {"cpu_baseline": cpu_decode_rate(shape, model.synthetic_tensors(shape, seed=1),
+                                                          model.prompt_tokens(shape, DECODE_PROMPT, seed=2))}
+        line["decode"]["tokens_per_s"] = line["decode"]["cpu_baseline"]["value"]
     print(json.dumps(line), flush=True)
     return 0
 
@@ -312,6 +414,10 @@ def run_ours(args) -> int:
         cpu = cpu_gemv_rate(threads, target_s=args.cpu_seconds)
         cpu.pop("median_s", None)
 
+    decode = None
+    if world == 1 and not args.no_decode:
+        decode = decode_leg(args, dev)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -333,6 +439,7 @@ def run_ours(args) -> int:
                       else "CUDA events around host-launched GEMVs",
             "clocks": clocks,
             "device_status": status,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     g.close()
@@ -439,6 +546,7 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-graph", action="store_true", help="launch each step from the host instead of a CUDA graph")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 1B decode tokens/s leg")
     ap.add_argument("--workload", choices=["gemv", "lmhead"], default="gemv",
                     help="gemv: Q4_K 14336x4096 GEMV per GPU (the headline); "
                          "lmhead: Q6_K 128256x4096 rows sharded over the GPUs + all-gather")
