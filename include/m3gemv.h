@@ -266,6 +266,22 @@ M3G_API void* m3g_decoder_stream(const m3g_decoder* dec);
 M3G_API int m3g_decoder_set_graph(m3g_decoder* dec, int use_graph);
 M3G_API void m3g_decoder_destroy(m3g_decoder* dec);
 
+/* ---------------------------------------------------------------- greedy head without allocation
+ *
+ * No counterpart in the reference.  *token (device memory) = the greedy pick
+ * of y = W x -- the lowest row index holding the largest value, the pick of
+ * sample_with_params with top_k = 1 -- computed by the tensor-core GEMV with
+ * its argmax epilogue.  Allocates no device memory: the logits and the
+ * reduction key live in a static device array of this library, so out_dim is
+ * at most 262144 (M3G_EINVAL beyond).  The first call on a device (with
+ * that device current) sets up that array's address; make it before any
+ * stream capture begins.  One call at a time per device: overlapping calls
+ * on different streams share the array and race.  *token = 0xFFFFFFFF when a
+ * bounded wait inside the GEMV gave up.  Enqueues on `stream` (NULL = the
+ * legacy default stream) and returns without waiting. */
+M3G_API int m3g_matvec_greedy_noalloc(const float* x, const uint8_t* raw, uint64_t raw_len, uint32_t dtype,
+                                      uint64_t in_dim, uint64_t out_dim, uint32_t* token, void* stream);
+
 /* ---------------------------------------------------------------- diagnostics */
 
 /* Error word the kernels of `device` set when a bounded wait gives up

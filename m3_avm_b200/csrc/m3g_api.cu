@@ -425,6 +425,35 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
   return M3G_OK;
 }
 
+// The greedy-pick GEMV (argmax epilogue into *key) planned from device
+// attributes alone, with a caller-provided status word: no per-device state
+// is created, so nothing is allocated.
+int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, float* y, long long in_dim,
+                   long long out_dim, cudaStream_t st, int sms, int smem_per_sm, int smem_optin, uint32_t* status,
+                   unsigned long long* key) {
+  FmtInfo f;
+  if (int rc = gemv_rules(dtype, raw_len, static_cast<uint64_t>(in_dim), static_cast<uint64_t>(out_dim), f)) return rc;
+  DevState ds;
+  ds.ready = true;
+  ds.sms = sms;
+  ds.smem_per_sm = smem_per_sm;
+  ds.smem_optin = smem_optin;
+  ds.status = status;
+  MmaPlan mp;
+  if (!plan_mma(f, in_dim, out_dim, w, x, ds, mp, false))
+    return fail(M3G_EINVAL, "no tensor-core plan for dtype %u, %lld x %lld (K %% 256, 16-byte rows and pointers)",
+                dtype, out_dim, in_dim);
+  mp.a.w = w;
+  mp.a.x = x;
+  mp.a.y = y;
+  mp.a.status = status;
+  mp.a.argmax_key = key;
+  cudaError_t e = launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "k_gemv_mma launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return M3G_OK;
+}
+
 int status_word(int device, uint32_t** out) {
   DevState* ds = nullptr;
   if (int rc = dev_state(device, &ds)) return rc;

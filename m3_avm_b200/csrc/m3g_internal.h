@@ -86,6 +86,12 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
                cudaStream_t st, bool decode, unsigned long long* argmax_key = nullptr);
 
+// GEMV with the greedy-pick epilogue, planned from the given device
+// attributes, reporting into the given status word (allocates nothing).
+int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, float* y, long long in_dim,
+                   long long out_dim, cudaStream_t st, int sms, int smem_per_sm, int smem_optin, uint32_t* status,
+                   unsigned long long* key);
+
 // The per-device status word the kernels set kStatus* bits in.
 int status_word(int device, uint32_t** out);
 

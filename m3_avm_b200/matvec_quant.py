@@ -122,3 +122,17 @@ def matvec_fused_dev(x, raw, dtype: int, in_dim: int, out_dim: int, xmode: int =
                                           raw.numel(), dtype, in_dim, out_dim, y.data_ptr(), ctypes.c_void_p(st))
     _lib.check(rc)
     return y
+
+
+def matvec_greedy_noalloc(x, raw, dtype: int, in_dim: int, out_dim: int, token=None, stream=None):
+    """Greedy pick of W x into a device uint32 (m3g_matvec_greedy_noalloc): the
+    library allocates nothing for it.  Returns the int32-typed token tensor."""
+    import torch
+
+    if token is None:
+        token = torch.empty(1, dtype=torch.int32, device=x.device)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+    rc = _lib.load().m3g_matvec_greedy_noalloc(x.data_ptr(), raw.data_ptr(), raw.numel(), dtype, in_dim, out_dim,
+                                               token.data_ptr(), ctypes.c_void_p(st))
+    _lib.check(rc)
+    return token
