@@ -205,10 +205,14 @@ M3G_API void m3g_shard_destroy(m3g_shard* ctx);
  *            src/inference.rs:1092-1097 (x = gate, x2 = up)
  *   res != NULL: y[j] = res[j] + (W x')[j], the residual adds of
  *            src/inference.rs:1083 and :1103 (res may equal y).
+ *   swiglu != 0: W holds gate and up rows interleaved in blocks of 8 (8 gate
+ *            rows, then the same 8 up rows; out_dim % 16 == 0) and y gets
+ *            out_dim/2 values silu(gate_i) * up_i (src/inference.rs:1092-1097);
+ *            not combined with res or xmode 2.
  * Needs in_dim % 256 == 0 and 16-byte rows (the tensor-core plan);
  * M3G_EINVAL otherwise.  Enqueues on `stream` (NULL = legacy default stream). */
 M3G_API int m3g_matvec_fused_dev(const float* x, const float* x2, const float* gamma, const float* res, int xmode,
-                                 const uint8_t* raw, uint64_t raw_len, uint32_t dtype, uint64_t in_dim,
+                                 int swiglu, const uint8_t* raw, uint64_t raw_len, uint32_t dtype, uint64_t in_dim,
                                  uint64_t out_dim, float* y, void* stream);
 
 /* ---------------------------------------------------------------- device-resident greedy decode

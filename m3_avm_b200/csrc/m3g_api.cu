@@ -390,8 +390,10 @@ bool block_geometry(uint32_t dtype, int* be, int* bb) {
 
 int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
-               cudaStream_t st, bool decode, unsigned long long* argmax_key) {
+               cudaStream_t st, bool decode, unsigned long long* argmax_key, bool swiglu) {
   const bool coresident = decode && g_tune.decode_coresident;
+  if (swiglu && (out_dim % 16 || xmode == kXSiluMul || res || argmax_key))
+    return fail(M3G_EINVAL, "SwiGLU epilogue needs gate/up rows in 16-row blocks and no other epilogue");
   FmtInfo f;
   if (int rc = gemv_rules(dtype, raw_len, static_cast<uint64_t>(in_dim), static_cast<uint64_t>(out_dim), f)) return rc;
   if (xmode < kXPlain || xmode > kXSiluMul) return fail(M3G_EINVAL, "unknown input transform %d", xmode);
@@ -417,6 +419,12 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
   mp.a.res = res;
   mp.a.xmode = xmode;
   mp.a.argmax_key = argmax_key;
+  mp.a.swiglu = swiglu ? 1 : 0;
+  if (swiglu) {  // tiles must start on 16-row (gate/up block) boundaries
+    const long long rpc = (mp.a.rows_per_cta + 15) / 16 * 16;
+    mp.a.rows_per_cta = static_cast<int>(rpc);
+    mp.grid = static_cast<int>((out_dim + rpc - 1) / rpc);
+  }
   mp.a.xfirst = static_cast<int>(decode ? g_tune.decode_xfirst : g_tune.mma_xfirst);
   if (decode) mp.a.PRE = static_cast<int>(g_tune.decode_pre);
   cudaError_t e = launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);

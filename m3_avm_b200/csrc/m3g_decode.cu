@@ -12,8 +12,9 @@
 //                     over positions [0, pos] per query head (GQA: head hh reads
 //                     KV head hh / (n_heads / n_kv_heads))
 //     GEMV  o         hidden += W_o att (residual fused in the epilogue)
-//     GEMV  gate|up   rms_norm(hidden) * ffn_norm input, gate|up rows concatenated
-//     GEMV  down      silu(gate) * up input, hidden += W_down (...)
+//     GEMV  gate|up   rms_norm(hidden) * ffn_norm input, gate and up rows
+//                     interleaved in blocks of 8 so the epilogue writes silu(g) * u
+//     GEMV  down      hidden += W_down (silu(g) * u)
 //   GEMV  head        rms_norm(hidden) * output_norm -> logits
 //                     whose epilogue also reduces (logit, row) to the greedy
 //                     pick with one 64-bit atomicMax per CTA
@@ -368,6 +369,25 @@ int concat_rows(m3g_decoder* d, const std::vector<const Tensor*>& parts, Gemv& g
   return M3G_OK;
 }
 
+// gate|up rows interleaved in blocks of 8 (8 gate rows, then the same 8 up
+// rows) for the GEMV's SwiGLU epilogue, which then writes silu(g) * u.
+int interleave_gate_up(m3g_decoder* d, const Tensor& gate, const Tensor& up, Gemv& g) {
+  g = Gemv{};
+  if (gate.dtype != up.dtype || gate.in != up.in || gate.out != up.out || gate.out % 8) return M3G_OK;
+  uint64_t need = 0;
+  if (m3g_quant_raw_len(gate.dtype, static_cast<uint64_t>(gate.in) * gate.out, &need)) return M3G_OK;
+  const uint64_t rb = need / static_cast<uint64_t>(gate.out);
+  if (rb * gate.out != need || rb % 16) return M3G_OK;  // rows must be whole, 16-byte multiples
+  uint8_t* buf = nullptr;
+  DEC_CUDA(cudaMalloc(&buf, 2 * need));
+  d->fused.push_back(buf);
+  const size_t blk = 8 * rb, nblk = static_cast<size_t>(gate.out / 8);
+  DEC_CUDA(cudaMemcpy2D(buf, 2 * blk, gate.d, blk, blk, nblk, cudaMemcpyDeviceToDevice));
+  DEC_CUDA(cudaMemcpy2D(buf + blk, 2 * blk, up.d, blk, blk, nblk, cudaMemcpyDeviceToDevice));
+  g = Gemv{buf, 2 * need, gate.dtype, gate.in, 2 * gate.out};
+  return M3G_OK;
+}
+
 int prepare(m3g_decoder* d) {
   if (d->prepared) return M3G_OK;
   for (size_t s = 0; s < d->t.size(); ++s)
@@ -378,15 +398,16 @@ int prepare(m3g_decoder* d) {
   for (int l = 0; l < L; ++l) {
     const Tensor* T = &d->t[kSlotLayer0 + kPerLayer * l];
     if (int rc = concat_rows(d, {&T[kQ], &T[kK], &T[kV]}, d->qkv[l])) return rc;
-    if (int rc = concat_rows(d, {&T[kGate], &T[kUp]}, d->gu[l])) return rc;
+    if (int rc = interleave_gate_up(d, T[kGate], T[kUp], d->gu[l])) return rc;
   }
   d->prepared = true;
   return M3G_OK;
 }
 
 int gemv(m3g_decoder* d, const Gemv& g, const float* x, const float* x2, const float* gamma, const float* res,
-         int xmode, float* y, unsigned long long* key = nullptr) {
-  return m3g::gemv_fused(d->device, g.dtype, g.w, g.len, x, x2, gamma, res, xmode, y, g.in, g.out, d->st, true, key);
+         int xmode, float* y, unsigned long long* key = nullptr, bool swiglu = false) {
+  return m3g::gemv_fused(d->device, g.dtype, g.w, g.len, x, x2, gamma, res, xmode, y, g.in, g.out, d->st, true, key,
+                         swiglu);
 }
 
 // Enqueue one decode step on d->st (also the body the graph captures).
@@ -434,14 +455,16 @@ int enqueue_step(m3g_decoder* d) {
       DEC_CUDA(m3g::launch_pdl(m3g::k_attention<128>, agrid, dim3(m3g::kAttnThreads), attn_smem, d->st, a));
     }
     if (int rc = gemv(d, part(T[kO]), d->att, nullptr, nullptr, d->hidden, m3g::kXPlain, d->hidden)) return rc;
-    if (d->gu[l].w) {
-      if (int rc = gemv(d, d->gu[l], d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, d->gub)) return rc;
-    } else {
+    if (d->gu[l].w) {  // interleaved gate|up: the epilogue writes silu(g) * u
+      if (int rc = gemv(d, d->gu[l], d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, d->gub, nullptr, true))
+        return rc;
+      if (int rc = gemv(d, part(T[kDown]), d->gub, nullptr, nullptr, d->hidden, m3g::kXPlain, d->hidden)) return rc;
+    } else {  // separate launches; the down GEMV applies SwiGLU to its input
       if (int rc = gemv(d, part(T[kGate]), d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, d->gub)) return rc;
       if (int rc = gemv(d, part(T[kUp]), d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, d->gub + F)) return rc;
+      if (int rc = gemv(d, part(T[kDown]), d->gub, d->gub + F, nullptr, d->hidden, m3g::kXSiluMul, d->hidden))
+        return rc;
     }
-    if (int rc = gemv(d, part(T[kDown]), d->gub, d->gub + F, nullptr, d->hidden, m3g::kXSiluMul, d->hidden))
-      return rc;
   }
   const float* g_out = reinterpret_cast<const float*>(d->t[kSlotOutNorm].d);
   if (int rc = gemv(d, part(d->t[kSlotOut]), d->hidden, nullptr, g_out, nullptr, m3g::kXRmsNorm, d->logits, d->key))
@@ -749,14 +772,14 @@ M3G_API void m3g_decoder_destroy(m3g_decoder* d) {
 
 // Fused GEMV with the decode step's input transforms and residual epilogue.
 M3G_API int m3g_matvec_fused_dev(const float* x, const float* x2, const float* gamma, const float* res, int xmode,
-                                 const uint8_t* raw, uint64_t raw_len, uint32_t dtype, uint64_t in_dim,
+                                 int swiglu, const uint8_t* raw, uint64_t raw_len, uint32_t dtype, uint64_t in_dim,
                                  uint64_t out_dim, float* y, void* stream) {
   if (!x || !raw || !y) return host_fail(M3G_EINVAL, "null argument");
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return host_fail(M3G_ECUDA, "no CUDA device");
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;
   return m3g::gemv_fused(dev, dtype, raw, raw_len, x, x2, gamma, res, xmode, y, static_cast<long long>(in_dim),
-                         static_cast<long long>(out_dim), st, false);
+                         static_cast<long long>(out_dim), st, false, nullptr, swiglu != 0);
 }
 
 }  // extern "C"

@@ -73,6 +73,10 @@ struct MmaArgs {
   // 1: stages past the first PRE are issued only after the consumers have
   // loaded x (their loads then do not wait behind the weight stream).
   int xfirst;
+  // 1: the rows are gate/up pairs in blocks of 8 gate rows then their 8 up
+  // rows; y[i] = silu(gate_i) * up_i (rows/2 outputs).  rows_per_cta is a
+  // multiple of 16.
+  int swiglu;
 };
 
 enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
@@ -84,7 +88,7 @@ enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
 // streaming their weights beside the running one.
 int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
-               cudaStream_t st, bool decode, unsigned long long* argmax_key = nullptr);
+               cudaStream_t st, bool decode, unsigned long long* argmax_key = nullptr, bool swiglu = false);
 
 // GEMV with the greedy-pick epilogue, planned from the given device
 // attributes, reporting into the given status word (allocates nothing).

@@ -504,18 +504,26 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
       if (s - grp * a.NKC == a.NKC - 1) {
         const int rows_g = min(SR, nrows - SR * grp);
         const float* rb = red + static_cast<size_t>(buf) * SR * WK;
+        float acc = 0.f;
         if (lane < rows_g) {
-          float acc = 0.f;
 #pragma unroll
           for (int w = 0; w < WK; ++w) acc += rb[lane * WK + w];
-          const long long r = row0 + SR * grp + lane;
-          if constexpr (FUSED) {
+        }
+        const long long r = row0 + SR * grp + lane;
+        if constexpr (FUSED) {
+          if (a.swiglu) {
+            // Rows come in blocks of 8 gate rows then the 8 matching up rows
+            // (every tile starts on a block boundary): h = silu(g) * u.
+            const float u = __shfl_down_sync(0xFFFFFFFFu, acc, 8);
+            if ((lane & 15) < 8 && lane < rows_g)
+              a.y[(r >> 4) * 8 + (r & 7)] = __fmul_rn(__fdividef(acc, 1.0f + __expf(-acc)), u);
+          } else if (lane < rows_g) {
             const float yv = a.res ? a.res[r] + acc : acc;
             a.y[r] = yv;
             if (a.argmax_key && yv == yv) best_key = max(best_key, argmax_key(yv, r));
-          } else {
-            a.y[r] = acc;
           }
+        } else if (lane < rows_g) {
+          a.y[r] = acc;
         }
       }
       __syncwarp();
@@ -790,7 +798,7 @@ static cudaError_t launch_mma_cfg(const MmaArgs& a, int tps, int wk, int grid, s
 template <class F>
 static cudaError_t launch_mma_fmt(const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
                                   bool pdl) {
-  const bool fused = a.xmode != kXPlain || a.res || a.argmax_key || a.xfirst;
+  const bool fused = a.xmode != kXPlain || a.res || a.argmax_key || a.xfirst || a.swiglu;
   return fused ? launch_mma_cfg<F, true>(a, tps, wk, grid, smem, st, pdl)
                : launch_mma_cfg<F, false>(a, tps, wk, grid, smem, st, pdl);
 }

@@ -109,17 +109,19 @@ X_PLAIN, X_RMSNORM, X_SILU_MUL = 0, 1, 2
 
 
 def matvec_fused_dev(x, raw, dtype: int, in_dim: int, out_dim: int, xmode: int = X_PLAIN, x2=None, gamma=None,
-                     res=None, y=None, stream=None):
+                     res=None, y=None, stream=None, swiglu: bool = False):
     """The decode step's fused GEMV over CUDA tensors (m3g_matvec_fused_dev):
-    y = W x' (+ res), x' = x, rms_norm(x) * gamma, or silu(x) * x2."""
+    y = W x' (+ res), x' = x, rms_norm(x) * gamma, or silu(x) * x2; with
+    swiglu, W is gate/up rows interleaved in blocks of 8 and y = silu(g) * u."""
     import torch
 
     if y is None:
-        y = torch.empty(out_dim, dtype=torch.float32, device=x.device)
+        y = torch.empty(out_dim // 2 if swiglu else out_dim, dtype=torch.float32, device=x.device)
     st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
     ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
-    rc = _lib.load().m3g_matvec_fused_dev(x.data_ptr(), ptr(x2), ptr(gamma), ptr(res), xmode, raw.data_ptr(),
-                                          raw.numel(), dtype, in_dim, out_dim, y.data_ptr(), ctypes.c_void_p(st))
+    rc = _lib.load().m3g_matvec_fused_dev(x.data_ptr(), ptr(x2), ptr(gamma), ptr(res), xmode, 1 if swiglu else 0,
+                                          raw.data_ptr(), raw.numel(), dtype, in_dim, out_dim, y.data_ptr(),
+                                          ctypes.c_void_p(st))
     _lib.check(rc)
     return y
 

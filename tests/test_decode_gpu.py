@@ -125,6 +125,36 @@ def test_fused_gemv_forms(torch_cuda, dtype, in_dim, out_dim, xmode):
         assert bad.size == 0, (with_res, bad[:5], np.abs(got - want)[bad[:5]], bound[bad[:5]])
 
 
+@pytest.mark.parametrize("dtype,in_dim,F", [(12, 2048, 8192), (8, 2048, 1000 // 8 * 8), (14, 2048, 512)])
+def test_fused_gemv_swiglu_epilogue(torch_cuda, dtype, in_dim, F):
+    torch = torch_cuda
+    from m3_avm_b200 import matvec_quant as MQ
+
+    gate = synth.weights(dtype, in_dim, F, seed=F + 1)
+    up = synth.weights(dtype, in_dim, F, seed=F + 2)
+    rb = gate.size // F
+    inter = np.concatenate([gate.reshape(F // 8, 8 * rb), up.reshape(F // 8, 8 * rb)], axis=1).reshape(-1)
+    x = synth.activations(in_dim, 9)
+    gamma = synth.activations(in_dim, 10)
+    xin = O.rms_norm(x, gamma)
+    g = O.matvec_quant(xin, gate, dtype, in_dim, F).astype(np.float64)
+    u = O.matvec_quant(xin, up, dtype, in_dim, F).astype(np.float64)
+    with np.errstate(over="ignore"):
+        want = g / (1.0 + np.exp(-g)) * u
+    dev = torch.device("cuda:0")
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    y = MQ.matvec_fused_dev(T(x), T(inter), dtype, in_dim, 2 * F, xmode=MQ.X_RMSNORM, gamma=T(gamma), swiglu=True)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy().astype(np.float64)
+    bg = O.gemv_bound(gate, dtype, in_dim, F, xin)
+    bu = O.gemv_bound(up, dtype, in_dim, F, xin)
+    with np.errstate(over="ignore"):
+        sil = np.abs(g / (1.0 + np.exp(-g)))
+    tol = 1.1 * bg * np.abs(u) + sil * bu + np.abs(want) * (np.abs(g) + 1.0) * 2.0 ** -20 + 1e-30
+    bad = np.nonzero(np.abs(got - want) > tol)[0]
+    assert bad.size == 0, (bad[:5], got[bad[:5]], want[bad[:5]], tol[bad[:5]])
+
+
 def test_fused_gemv_rejects_shapes_without_tensor_core_plan(torch_cuda):
     torch = torch_cuda
     from m3_avm_b200 import _lib
