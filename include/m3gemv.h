@@ -240,6 +240,17 @@ typedef struct {
 } m3g_decoder_config;
 
 M3G_API int m3g_decoder_create(int device, const m3g_decoder_config* cfg, m3g_decoder** out);
+/* The same engine sharded over `world` ranks (one process per GPU) sharing
+ * one NCCL unique id (m3g_shard_unique_id): each rank keeps the attention
+ * weights whole and rows [r*ffn/world, ...) of ffn_gate and ffn_up, rows
+ * [r*hidden/world, ...) of ffn_down and rows [r*ceil(vocab/world), ...) of
+ * output; uploads still pass the full tensors.  Each step adds two in-place
+ * all-gathers per layer and one 64-bit MAX all-reduce of the greedy key.
+ * Needs ffn % (8*world) == 0, hidden % world == 0, gate and up of one dtype.
+ * Creation gives up with M3G_ETIMEOUT when a rank does not join within
+ * timeout_s.  Every rank must issue the same calls in the same order. */
+M3G_API int m3g_decoder_create_sharded(int device, const m3g_decoder_config* cfg, int rank, int world,
+                                       const uint8_t* nccl_id128, double timeout_s, m3g_decoder** out);
 /* Copies one tensor to HBM (replacing an earlier upload of the slot). */
 M3G_API int m3g_decoder_upload(m3g_decoder* dec, uint32_t slot, uint32_t dtype, const void* raw, uint64_t raw_len);
 /* forward_one(token): one step at the current position; vocab logits to the

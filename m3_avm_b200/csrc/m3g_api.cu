@@ -390,7 +390,7 @@ bool block_geometry(uint32_t dtype, int* be, int* bb) {
 
 int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
-               cudaStream_t st, bool decode, unsigned long long* argmax_key, bool swiglu) {
+               cudaStream_t st, bool decode, unsigned long long* argmax_key, bool swiglu, long long key_row0) {
   const bool coresident = decode && g_tune.decode_coresident;
   if (swiglu && (out_dim % 16 || xmode == kXSiluMul || res || argmax_key))
     return fail(M3G_EINVAL, "SwiGLU epilogue needs gate/up rows in 16-row blocks and no other epilogue");
@@ -420,6 +420,7 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
   mp.a.xmode = xmode;
   mp.a.argmax_key = argmax_key;
   mp.a.swiglu = swiglu ? 1 : 0;
+  mp.a.key_row0 = key_row0;
   if (swiglu) {  // tiles must start on 16-row (gate/up block) boundaries
     const long long rpc = (mp.a.rows_per_cta + 15) / 16 * 16;
     mp.a.rows_per_cta = static_cast<int>(rpc);

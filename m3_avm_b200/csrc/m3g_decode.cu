@@ -22,18 +22,27 @@
 //                     tokens[pos + 1] unless that slot holds a given prompt
 //                     token, then pos += 1
 //
+// Sharded over the GPUs of a node (one process per GPU, one NCCL
+// communicator), each rank keeps the attention weights whole and only its
+// rows of gate/up, down and the vocab head: after gate|up one in-place
+// all-gather assembles silu(g) * u, after down one assembles the hidden
+// state, and one 64-bit MAX all-reduce merges the ranks' greedy keys.  Every
+// row is computed exactly as on one GPU, so the ranks hold identical state.
+//
 // The position and the token stream live in device memory, so one captured
 // CUDA graph replays every step; kernels chain with programmatic dependent
 // launch so each GEMV starts streaming its weights while the previous kernel
 // finishes.  The KV cache is compact (n_kv_heads * head_dim floats per
 // position and layer); the reference stores it repeated to the full hidden
 // width, which holds the same values.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <vector>
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include "../../include/m3gemv.h"
 #include "m3g_device.cuh"
@@ -43,6 +52,9 @@
 namespace m3g {
 int host_fail(int code, const char* fmt, ...);
 bool block_geometry(uint32_t dtype, int* be, int* bb);
+int nccl_settle(ncclComm_t comm, ncclResult_t r, const char* what, double timeout_s);
+int nccl_comm_create(int rank, int world, const uint8_t* id128, double timeout_s, ncclComm_t* out);
+void nccl_comm_close(ncclComm_t comm, double timeout_s);
 }  // namespace m3g
 
 namespace m3g {
@@ -270,7 +282,8 @@ struct Tensor {
   uint8_t* d = nullptr;  // device bytes (norms: f32)
   uint64_t len = 0;
   uint32_t dtype = 0;
-  int in = 0, out = 0;   // matrix shape; norms: in = out = hidden
+  int in = 0, out = 0;   // matrix shape held here (a row shard's rows); norms: in = out = hidden
+  int row0 = 0;          // first row of the full tensor held here
   bool set = false;
 };
 
@@ -287,6 +300,10 @@ struct Gemv {
 
 struct m3g_decoder {
   int device = 0;
+  int rank = 0, world = 1;
+  ncclComm_t comm = nullptr;
+  double timeout_s = 60.0;
+  int Fr = 0, hr = 0, Vr = 0;  // rows per rank of gate/up (each), down, head
   m3g_decoder_config cfg{};
   int hd = 0, kvd = 0;
   cudaStream_t st = nullptr;
@@ -337,6 +354,27 @@ int slot_shape(const m3g_decoder* d, int slot, int* in, int* out, bool* is_norm)
 }
 
 bool gemv_dtype(uint32_t dt) { return dt == 2 || dt == 8 || dt == 12 || dt == 13 || dt == 14; }
+
+// Rows [row0, row0 + rows) of a slot's full tensor that this rank keeps.
+void shard_rows(const m3g_decoder* d, int slot, int full_out, int* row0, int* rows) {
+  *row0 = 0;
+  *rows = full_out;
+  if (d->world == 1 || slot < kSlotLayer0) {
+    if (slot == kSlotOut && d->world > 1) {
+      *row0 = d->rank * d->Vr;
+      *rows = std::max(0, std::min(full_out, *row0 + d->Vr) - *row0);
+    }
+    return;
+  }
+  const int kind = (slot - kSlotLayer0) % kPerLayer;
+  if (kind == kGate || kind == kUp) {
+    *row0 = d->rank * d->Fr;
+    *rows = d->Fr;
+  } else if (kind == kDown) {
+    *row0 = d->rank * d->hr;
+    *rows = d->hr;
+  }
+}
 
 Gemv part(const Tensor& x) { return Gemv{x.d, x.len, x.dtype, x.in, x.out}; }
 
@@ -399,6 +437,8 @@ int prepare(m3g_decoder* d) {
     const Tensor* T = &d->t[kSlotLayer0 + kPerLayer * l];
     if (int rc = concat_rows(d, {&T[kQ], &T[kK], &T[kV]}, d->qkv[l])) return rc;
     if (int rc = interleave_gate_up(d, T[kGate], T[kUp], d->gu[l])) return rc;
+    if (d->world > 1 && !d->gu[l].w)
+      return host_fail(M3G_EINVAL, "sharded decode needs gate and up of one dtype with 16-byte rows (layer %d)", l);
   }
   d->prepared = true;
   return M3G_OK;
@@ -455,7 +495,19 @@ int enqueue_step(m3g_decoder* d) {
       DEC_CUDA(m3g::launch_pdl(m3g::k_attention<128>, agrid, dim3(m3g::kAttnThreads), attn_smem, d->st, a));
     }
     if (int rc = gemv(d, part(T[kO]), d->att, nullptr, nullptr, d->hidden, m3g::kXPlain, d->hidden)) return rc;
-    if (d->gu[l].w) {  // interleaved gate|up: the epilogue writes silu(g) * u
+    if (d->world > 1) {  // this rank's rows, then all-gathers of silu(g) * u and of hidden
+      float* hslot = d->gub + static_cast<size_t>(d->rank) * d->Fr;
+      if (int rc = gemv(d, d->gu[l], d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, hslot, nullptr, true))
+        return rc;
+      if (int rc = m3g::nccl_settle(d->comm, ncclAllGather(hslot, d->gub, d->Fr, ncclFloat, d->comm, d->st),
+                                    "ncclAllGather(ffn)", d->timeout_s))
+        return rc;
+      float* yslot = d->hidden + static_cast<size_t>(d->rank) * d->hr;
+      if (int rc = gemv(d, part(T[kDown]), d->gub, nullptr, nullptr, yslot, m3g::kXPlain, yslot)) return rc;
+      if (int rc = m3g::nccl_settle(d->comm, ncclAllGather(yslot, d->hidden, d->hr, ncclFloat, d->comm, d->st),
+                                    "ncclAllGather(hidden)", d->timeout_s))
+        return rc;
+    } else if (d->gu[l].w) {  // interleaved gate|up: the epilogue writes silu(g) * u
       if (int rc = gemv(d, d->gu[l], d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, d->gub, nullptr, true))
         return rc;
       if (int rc = gemv(d, part(T[kDown]), d->gub, nullptr, nullptr, d->hidden, m3g::kXPlain, d->hidden)) return rc;
@@ -467,8 +519,17 @@ int enqueue_step(m3g_decoder* d) {
     }
   }
   const float* g_out = reinterpret_cast<const float*>(d->t[kSlotOutNorm].d);
-  if (int rc = gemv(d, part(d->t[kSlotOut]), d->hidden, nullptr, g_out, nullptr, m3g::kXRmsNorm, d->logits, d->key))
-    return rc;
+  const Tensor& H = d->t[kSlotOut];
+  if (H.out > 0) {  // the last rank of a small vocabulary may hold no rows
+    if (int rc = m3g::gemv_fused(d->device, H.dtype, H.d, H.len, d->hidden, nullptr, g_out, nullptr, m3g::kXRmsNorm,
+                                 d->logits + H.row0, H.in, H.out, d->st, true, d->key, false, H.row0))
+      return rc;
+  }
+  if (d->world > 1) {  // the greedy pick over all ranks' rows
+    if (int rc = m3g::nccl_settle(d->comm, ncclAllReduce(d->key, d->key, 1, ncclUint64, ncclMax, d->comm, d->st),
+                                  "ncclAllReduce(greedy key)", d->timeout_s))
+      return rc;
+  }
   DEC_CUDA(m3g::launch_pdl(m3g::k_pick_step, dim3(1), dim3(32), 0, d->st, d->key, d->dpos, d->tokens,
                            static_cast<const int*>(d->nfixed), mp, d->last));
   return M3G_OK;
@@ -527,6 +588,15 @@ int check_status(m3g_decoder* d) {
   return M3G_OK;
 }
 
+// Sharded: every rank assembles the full logits of the last step (only when
+// the caller asks for them; the greedy loop needs only the merged key).
+int gather_logits(m3g_decoder* d, bool want) {
+  if (d->world == 1 || !want) return M3G_OK;
+  float* slot = d->logits + static_cast<size_t>(d->rank) * d->Vr;
+  return m3g::nccl_settle(d->comm, ncclAllGather(slot, d->logits, d->Vr, ncclFloat, d->comm, d->st),
+                          "ncclAllGather(logits)", d->timeout_s);
+}
+
 struct DevGuard {
   int prev = -1;
   explicit DevGuard(int dev) {
@@ -543,8 +613,17 @@ struct DevGuard {
 extern "C" {
 
 M3G_API int m3g_decoder_create(int device, const m3g_decoder_config* cfg, m3g_decoder** out) {
+  return m3g_decoder_create_sharded(device, cfg, 0, 1, nullptr, 0.0, out);
+}
+
+M3G_API int m3g_decoder_create_sharded(int device, const m3g_decoder_config* cfg, int rank, int world,
+                                       const uint8_t* nccl_id128, double timeout_s, m3g_decoder** out) {
   if (!cfg || !out) return host_fail(M3G_EINVAL, "null argument");
   *out = nullptr;
+  if (world < 1 || rank < 0 || rank >= world) return host_fail(M3G_EINVAL, "rank %d of %d", rank, world);
+  if (world > 1 && !nccl_id128) return host_fail(M3G_EINVAL, "sharded decoder needs an NCCL unique id");
+  if (world > 1 && (cfg->ffn % (8ull * world) || cfg->hidden % world || cfg->vocab < static_cast<uint64_t>(world)))
+    return host_fail(M3G_EINVAL, "sharding needs ffn %% (8 * world) == 0 and hidden %% world == 0");
   const m3g_decoder_config& c = *cfg;
   if (!c.n_layers || !c.hidden || !c.ffn || !c.n_heads || !c.n_kv_heads || !c.vocab || !c.max_pos)
     return host_fail(M3G_EINVAL, "zero dimension in the decoder shape");
@@ -563,6 +642,12 @@ M3G_API int m3g_decoder_create(int device, const m3g_decoder_config* cfg, m3g_de
   auto* d = new m3g_decoder();
   d->device = device;
   d->cfg = c;
+  d->rank = rank;
+  d->world = world;
+  d->timeout_s = timeout_s > 0 ? timeout_s : 60.0;
+  d->Fr = static_cast<int>(c.ffn / world);
+  d->hr = static_cast<int>(c.hidden / world);
+  d->Vr = static_cast<int>((c.vocab + world - 1) / world);
   d->hd = static_cast<int>(hd);
   d->kvd = static_cast<int>(c.n_kv_heads * hd);
   d->t.resize(kSlotLayer0 + kPerLayer * c.n_layers);
@@ -581,7 +666,7 @@ M3G_API int m3g_decoder_create(int device, const m3g_decoder_config* cfg, m3g_de
   if (e == cudaSuccess) e = cudaMalloc(&d->qkvb, 4 * (h + 2 * d->kvd));
   if (e == cudaSuccess) e = cudaMalloc(&d->att, 4 * h);
   if (e == cudaSuccess) e = cudaMalloc(&d->gub, 4 * 2 * F);
-  if (e == cudaSuccess) e = cudaMalloc(&d->logits, 4 * c.vocab);
+  if (e == cudaSuccess) e = cudaMalloc(&d->logits, 4 * static_cast<size_t>(d->Vr) * world);
   if (e == cudaSuccess) e = cudaMalloc(&d->rope, 4 * mp * hd);
   if (e == cudaSuccess) e = cudaMalloc(&d->kc, 4 * c.n_layers * mp * d->kvd);
   if (e == cudaSuccess) e = cudaMalloc(&d->vc, 4 * c.n_layers * mp * d->kvd);
@@ -617,6 +702,9 @@ M3G_API int m3g_decoder_create(int device, const m3g_decoder_config* cfg, m3g_de
                                         static_cast<int>(attn_smem));
   }
   if (e != cudaSuccess) return fail(host_fail(M3G_ECUDA, "decoder setup: %s", cudaGetErrorString(e)));
+  if (world > 1) {
+    if (int rc = m3g::nccl_comm_create(rank, world, nccl_id128, d->timeout_s, &d->comm)) return fail(rc);
+  }
   *out = d;
   return M3G_OK;
 }
@@ -641,6 +729,13 @@ M3G_API int m3g_decoder_upload(m3g_decoder* d, uint32_t slot, uint32_t dtype, co
   if (raw_len < need)
     return host_fail(M3G_EINVAL, "slot %u: %llu bytes, needs %llu", slot, static_cast<unsigned long long>(raw_len),
                      static_cast<unsigned long long>(need));
+  int row0 = 0, rows = out;
+  shard_rows(d, static_cast<int>(slot), out, &row0, &rows);
+  const uint64_t rb = norm ? need : need / static_cast<uint64_t>(out);
+  if (!norm && rb * static_cast<uint64_t>(out) != need && rows != out)
+    return host_fail(M3G_EINVAL, "slot %u: rows of dtype %u straddle blocks and cannot be sharded", slot, dtype);
+  const uint64_t off = norm ? 0 : rb * static_cast<uint64_t>(row0);
+  const uint64_t len = norm ? need : (rows == out ? need : rb * static_cast<uint64_t>(rows));
   DevGuard g(d->device);
   if (cudaStreamSynchronize(d->st) != cudaSuccess) return host_fail(M3G_ECUDA, "decoder stream failed");
   drop_graph(d);
@@ -651,10 +746,12 @@ M3G_API int m3g_decoder_upload(m3g_decoder* d, uint32_t slot, uint32_t dtype, co
   if (t.d) cudaFree(t.d);
   t.d = nullptr;
   t.set = false;
-  DEC_CUDA(cudaMalloc(&t.d, need));
-  DEC_CUDA(cudaMemcpy(t.d, raw, need, cudaMemcpyHostToDevice));
-  t.len = need;
+  DEC_CUDA(cudaMalloc(&t.d, len ? len : 16));
+  if (len) DEC_CUDA(cudaMemcpy(t.d, static_cast<const uint8_t*>(raw) + off, len, cudaMemcpyHostToDevice));
+  t.len = len;
   t.dtype = dtype;
+  t.row0 = row0;
+  if (!norm) t.out = rows;
   t.set = true;
   return M3G_OK;
 }
@@ -670,6 +767,7 @@ M3G_API int m3g_decoder_forward(m3g_decoder* d, uint32_t token, float* logits) {
   DEC_CUDA(cudaMemcpyAsync(d->tokens + d->pos, &d->h_io[0], 4, cudaMemcpyHostToDevice, d->st));
   DEC_CUDA(cudaMemcpyAsync(d->nfixed, &d->h_io[1], 4, cudaMemcpyHostToDevice, d->st));
   if (int rc = run_steps(d, 1)) return rc;
+  if (int rc = gather_logits(d, logits != nullptr)) return rc;
   if (logits) DEC_CUDA(cudaMemcpyAsync(logits, d->logits, 4 * d->cfg.vocab, cudaMemcpyDeviceToHost, d->st));
   return check_status(d);
 }
@@ -686,6 +784,7 @@ M3G_API int m3g_decoder_prefill(m3g_decoder* d, const uint32_t* tokens, uint64_t
   const int nfixed = d->pos + static_cast<int>(n);
   DEC_CUDA(cudaMemcpy(d->nfixed, &nfixed, 4, cudaMemcpyHostToDevice));
   if (int rc = run_steps(d, n)) return rc;
+  if (int rc = gather_logits(d, logits != nullptr)) return rc;
   if (logits) DEC_CUDA(cudaMemcpyAsync(logits, d->logits, 4 * d->cfg.vocab, cudaMemcpyDeviceToHost, d->st));
   return check_status(d);
 }
@@ -756,7 +855,9 @@ M3G_API void m3g_decoder_destroy(m3g_decoder* d) {
   if (!d) return;
   DevGuard g(d->device);
   if (d->st) cudaStreamSynchronize(d->st);
-  drop_graph(d);
+  drop_graph(d);  // the graph holds NCCL work: released before the communicator
+  if (d->comm) m3g::nccl_comm_close(d->comm, d->timeout_s);
+  d->comm = nullptr;
   for (Tensor& t : d->t)
     if (t.d) cudaFree(t.d);
   for (uint8_t* f : d->fused) cudaFree(f);

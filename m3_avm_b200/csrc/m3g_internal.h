@@ -77,6 +77,8 @@ struct MmaArgs {
   // rows; y[i] = silu(gate_i) * up_i (rows/2 outputs).  rows_per_cta is a
   // multiple of 16.
   int swiglu;
+  // Row number the argmax key reports for local row 0 (a row shard's offset).
+  long long key_row0;
 };
 
 enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
@@ -88,7 +90,8 @@ enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
 // streaming their weights beside the running one.
 int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
-               cudaStream_t st, bool decode, unsigned long long* argmax_key = nullptr, bool swiglu = false);
+               cudaStream_t st, bool decode, unsigned long long* argmax_key = nullptr, bool swiglu = false,
+               long long key_row0 = 0);
 
 // GEMV with the greedy-pick epilogue, planned from the given device
 // attributes, reporting into the given status word (allocates nothing).

@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
           } else if (lane < rows_g) {
             const float yv = a.res ? a.res[r] + acc : acc;
             a.y[r] = yv;
-            if (a.argmax_key && yv == yv) best_key = max(best_key, argmax_key(yv, r));
+            if (a.argmax_key && yv == yv) best_key = max(best_key, argmax_key(yv, r + a.key_row0));
           }
         } else if (lane < rows_g) {
           a.y[r] = acc;

@@ -41,6 +41,10 @@ int nccl_fail(ncclResult_t r, const char* what) {
   return m3g::host_fail(M3G_ENCCL, "%s: %s", what, ncclGetErrorString(r));
 }
 
+}  // namespace
+
+namespace m3g {
+
 // The communicator is non-blocking (so that a missing rank cannot hang
 // creation): a call may return ncclInProgress, which is completed here by
 // polling the communicator's state for at most timeout_s seconds.
@@ -59,7 +63,58 @@ int nccl_settle(ncclComm_t comm, ncclResult_t r, const char* what, double timeou
   }
 }
 
-}  // namespace
+// A non-blocking communicator on the current device; a rank that never joins
+// makes creation abort after timeout_s with M3G_ETIMEOUT.
+int nccl_comm_create(int rank, int world, const uint8_t* id128, double timeout_s, ncclComm_t* out) {
+  *out = nullptr;
+  ncclUniqueId id;
+  memcpy(id.internal, id128, NCCL_UNIQUE_ID_BYTES);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
+  const auto t0 = std::chrono::steady_clock::now();
+  while (r == ncclInProgress || (r == ncclSuccess && comm)) {
+    ncclResult_t st = ncclInProgress;
+    if (ncclCommGetAsyncError(comm, &st) != ncclSuccess) {
+      r = ncclInternalError;
+      break;
+    }
+    if (st == ncclSuccess) {
+      r = ncclSuccess;
+      break;
+    }
+    if (st != ncclInProgress) {
+      r = st;
+      break;
+    }
+    const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (dt > timeout_s) {
+      ncclCommAbort(comm);
+      return m3g::host_fail(M3G_ETIMEOUT, "NCCL communicator init did not complete within %.1f s", timeout_s);
+    }
+    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+  }
+  if (r != ncclSuccess) {
+    if (comm) ncclCommAbort(comm);
+    return nccl_fail(r, "ncclCommInitRankConfig");
+  }
+  *out = comm;
+  return M3G_OK;
+}
+
+// Finalize (bounded) then destroy; abort when finalising does not complete.
+void nccl_comm_close(ncclComm_t comm, double timeout_s) {
+  if (!comm) return;
+  if (nccl_settle(comm, ncclCommFinalize(comm), "ncclCommFinalize", timeout_s) == M3G_OK)
+    ncclCommDestroy(comm);
+  else
+    ncclCommAbort(comm);
+}
+
+}  // namespace m3g
+
+using m3g::nccl_settle;
 
 struct m3g_shard {
   int device = 0, rank = 0, world = 1;
@@ -148,38 +203,9 @@ int m3g_shard_create(int device, int rank, int world, const uint8_t* id128, uint
   c->max_in = max_in;
   c->max_out = max_out;
   c->timeout_s = timeout_s;
-  ncclUniqueId id;
-  memcpy(id.internal, id128, NCCL_UNIQUE_ID_BYTES);
-  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
-  cfg.blocking = 0;
-  ncclResult_t r = ncclCommInitRankConfig(&c->comm, world, id, rank, &cfg);
-  const auto t0 = std::chrono::steady_clock::now();
-  while (r == ncclInProgress || (r == ncclSuccess && c->comm)) {
-    ncclResult_t st = ncclInProgress;
-    if (ncclCommGetAsyncError(c->comm, &st) != ncclSuccess) {
-      r = ncclInternalError;
-      break;
-    }
-    if (st == ncclSuccess) {
-      r = ncclSuccess;
-      break;
-    }
-    if (st != ncclInProgress) {
-      r = st;
-      break;
-    }
-    const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-    if (dt > timeout_s) {
-      ncclCommAbort(c->comm);
-      delete c;
-      return m3g::host_fail(M3G_ETIMEOUT, "NCCL communicator init did not complete within %.1f s", timeout_s);
-    }
-    std::this_thread::sleep_for(std::chrono::milliseconds(1));
-  }
-  if (r != ncclSuccess) {
-    if (c->comm) ncclCommAbort(c->comm);
+  if (int rc = m3g::nccl_comm_create(rank, world, id128, timeout_s, &c->comm)) {
     delete c;
-    return nccl_fail(r, "ncclCommInitRankConfig");
+    return rc;
   }
   cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
   if (e != cudaSuccess) {

@@ -18,15 +18,44 @@ from . import _lib, model
 
 
 class GpuDecoder:
-    def __init__(self, shape: model.LlamaShape, max_pos: int = 1024, device: int = 0):
+    """One engine per GPU.  With world > 1 the ranks (one process each) pass
+    the same 128-byte NCCL id (``sharded.unique_id()``) and make the same calls
+    in the same order; ffn_gate/up/down and the vocab head are row-sharded."""
+
+    def __init__(self, shape: model.LlamaShape, max_pos: int = 1024, device: int = 0, rank: int = 0,
+                 world: int = 1, nccl_id: bytes | None = None, timeout_s: float = 60.0):
         self.shape = shape
         self.max_pos = max_pos
         self.device = device
+        self.rank, self.world = rank, world
         cfg = _lib.DecoderConfig(shape.n_layers, shape.hidden, shape.ffn, shape.n_heads, shape.n_kv_heads,
                                  shape.vocab, max_pos, shape.rope_theta)
         h = ctypes.c_void_p()
-        _lib.check(_lib.load().m3g_decoder_create(device, ctypes.byref(cfg), ctypes.byref(h)))
+        if world == 1:
+            rc = _lib.load().m3g_decoder_create(device, ctypes.byref(cfg), ctypes.byref(h))
+        else:
+            if nccl_id is None or len(nccl_id) != 128:
+                raise ValueError("a sharded decoder needs the 128-byte NCCL unique id")
+            idbuf = (ctypes.c_uint8 * 128).from_buffer_copy(nccl_id)
+            rc = _lib.load().m3g_decoder_create_sharded(device, ctypes.byref(cfg), rank, world,
+                                                        ctypes.cast(idbuf, ctypes.c_void_p), float(timeout_s),
+                                                        ctypes.byref(h))
+        _lib.check(rc)
         self._h = h
+
+    @classmethod
+    def from_torch_dist(cls, shape: model.LlamaShape, max_pos: int = 1024, device: int = 0, timeout_s: float = 60.0):
+        """Join the ranks of an initialised torch.distributed group (rank 0's id is broadcast)."""
+        import torch.distributed as dist
+
+        from . import sharded
+
+        rank, world = dist.get_rank(), dist.get_world_size()
+        if world == 1:
+            return cls(shape, max_pos, device)
+        obj = [sharded.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        return cls(shape, max_pos, device, rank, world, obj[0], timeout_s)
 
     # ------------------------------------------------------------ weights
     def upload(self, slot: int, arr, dtype: int) -> None:
