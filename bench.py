@@ -153,12 +153,15 @@ def cpu_gemv_rate(threads: int, target_s: float, max_calls: int | None = None) -
 DECODE_PROMPT, DECODE_GEN = 128, 256
 
 
-def decode_leg(args, dev) -> dict:
+def decode_leg(args, dev, world: int = 1) -> dict:
     """Greedy decode of the Llama-3.2-1B-shaped model (16 layers, hidden 2048,
     FFN 8192, 32/8 heads x 64, vocab 128256, Q4_K attention/gate/up/embedding,
     Q6_K down and head), seeded synthetic weights: a 128-token prompt, then
-    256 generated tokens, all steps device-resident."""
+    256 generated tokens, all steps device-resident.  Under torchrun the
+    engine is row-sharded over the ranks (FFN and head, NCCL all-gathers) and
+    the time is the max over ranks (strong scaling: one model)."""
     import torch
+    import torch.distributed as dist
 
     from m3_avm_b200 import model
     from m3_avm_b200.decoder import GpuDecoder
@@ -166,8 +169,13 @@ def decode_leg(args, dev) -> dict:
     shape = model.LLAMA_1B
     tensors = model.synthetic_tensors(shape, seed=1)
     prompt = model.prompt_tokens(shape, DECODE_PROMPT, seed=2)
-    dec = GpuDecoder(shape, max_pos=DECODE_PROMPT + DECODE_GEN + 8, device=dev.index or 0)
+    max_pos = DECODE_PROMPT + DECODE_GEN + 8
+    if world > 1:
+        dec = GpuDecoder.from_torch_dist(shape, max_pos=max_pos, device=dev.index or 0, timeout_s=120)
+    else:
+        dec = GpuDecoder(shape, max_pos=max_pos, device=dev.index or 0)
     dec.upload_all(tensors)
+    exchange = dec.exchange
     dec.set_graph(not args.no_graph)
     st = torch.cuda.ExternalStream(dec.stream, device=dev)
     # warm-up: one full prompt + a few steps (graph capture, lazy setup)
@@ -176,6 +184,8 @@ def decode_leg(args, dev) -> dict:
     dec.sync()
     dec.clear_kv_cache()
     dec.prefill_logits(prompt)
+    if world > 1:
+        dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(st)
@@ -183,13 +193,23 @@ def decode_leg(args, dev) -> dict:
     e1.record(st)
     dec.sync()
     gen_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([gen_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gen_ms = float(t.item())
     toks = dec.tokens(DECODE_PROMPT, DECODE_GEN)
     tok_s = (DECODE_GEN - 1) / (gen_ms / 1e3)
     # e2e: the public call a user makes, host prompt in, host tokens out
     dec.clear_kv_cache()
+    if world > 1:
+        dist.barrier()
     t0 = time.perf_counter()
     toks2 = dec.generate(prompt, DECODE_GEN)
     e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
     dec.close()
     bytes_tok = shape.weight_bytes_per_token()
     peaks, kind = measured_peaks()
@@ -211,8 +231,15 @@ def decode_leg(args, dev) -> dict:
         "tokens_match_e2e": bool((toks == toks2).all()),
         "graph": not args.no_graph,
         "gpu_launches_per_token": 1 + 5 * shape.n_layers + 2,
+        "n_gpus": world,
+        "parallelism": f"rows{world} (ffn + head sharded, rows exchanged by {exchange})" if world > 1
+                       else "single GPU",
+        "scaling": "strong",
     }
-    if not args.no_cpu:
+    if world > 1:
+        out["nccl_collectives_per_token"] = 2 * shape.n_layers + 1
+        out["roofline"]["note"] = "weight bytes of the whole model per token; each GPU streams its share"
+    if not args.no_cpu and world == 1:
         out["cpu_baseline"] = cpu_decode_rate(shape, tensors, prompt)
     return out
 
@@ -415,8 +442,8 @@ def run_ours(args) -> int:
         cpu.pop("median_s", None)
 
     decode = None
-    if world == 1 and not args.no_decode:
-        decode = decode_leg(args, dev)
+    if not args.no_decode:
+        decode = decode_leg(args, dev, world)
 
     if rank == 0:
         line = {

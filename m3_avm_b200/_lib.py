@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple] = {
     "m3g_decoder_pos": (_u64, [_vp]),
     "m3g_decoder_truncate": (ctypes.c_int, [_vp, _u64]),
     "m3g_decoder_logits_dev": (_vp, [_vp]),
+    "m3g_decoder_exchange": (ctypes.c_int, [_vp]),
     "m3g_decoder_stream": (_vp, [_vp]),
     "m3g_decoder_set_graph": (ctypes.c_int, [_vp, ctypes.c_int]),
     "m3g_decoder_destroy": (None, [_vp]),

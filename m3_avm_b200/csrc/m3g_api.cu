@@ -91,6 +91,7 @@ struct Tuning {
   int64_t decode_pre = 1;         // mma_pre for the GEMVs of a decode step
   int64_t mma_xfirst = 0;         // issue the ring past PRE only once x is loaded
   int64_t decode_xfirst = 0;      // the same for the GEMVs of a decode step
+  int64_t decode_p2p = 1;         // sharded decode: peer stores over NVLink instead of NCCL all-gathers
 };
 Tuning g_tune;
 
@@ -390,7 +391,8 @@ bool block_geometry(uint32_t dtype, int* be, int* bb) {
 
 int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
-               cudaStream_t st, bool decode, unsigned long long* argmax_key, bool swiglu, long long key_row0) {
+               cudaStream_t st, bool decode, unsigned long long* argmax_key, bool swiglu, long long key_row0,
+               const PeerIO* peers, int* grid_out) {
   const bool coresident = decode && g_tune.decode_coresident;
   if (swiglu && (out_dim % 16 || xmode == kXSiluMul || res || argmax_key))
     return fail(M3G_EINVAL, "SwiGLU epilogue needs gate/up rows in 16-row blocks and no other epilogue");
@@ -428,6 +430,19 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
   }
   mp.a.xfirst = static_cast<int>(decode ? g_tune.decode_xfirst : g_tune.mma_xfirst);
   if (decode) mp.a.PRE = static_cast<int>(g_tune.decode_pre);
+  if (peers) {
+    for (int p = 0; p < kMaxPeers; ++p) {
+      mp.a.peer_y[p] = peers->peer_y[p];
+      mp.a.peer_key[p] = peers->peer_key[p];
+      mp.a.peer_cnt[p] = peers->peer_cnt[p];
+    }
+    mp.a.npeer = peers->npeer;
+    mp.a.done_cnt = peers->done_cnt;
+    mp.a.step = peers->step;
+    mp.a.wait_cnt = peers->wait_cnt;
+    mp.a.wait_mul = peers->wait_mul;
+  }
+  if (grid_out) *grid_out = mp.grid;
   cudaError_t e = launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);
   if (e != cudaSuccess) return cuda_fail(e, "k_gemv_mma launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -462,6 +477,8 @@ int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const flo
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return M3G_OK;
 }
+
+bool decode_p2p_enabled() { return g_tune.decode_p2p != 0; }
 
 int status_word(int device, uint32_t** out) {
   DevState* ds = nullptr;
@@ -510,6 +527,7 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "decode_pre") && value >= 0 && value <= 8) g_tune.decode_pre = value;
   else if (!strcmp(key, "mma_xfirst")) g_tune.mma_xfirst = value != 0;
   else if (!strcmp(key, "decode_xfirst")) g_tune.decode_xfirst = value != 0;
+  else if (!strcmp(key, "decode_p2p")) g_tune.decode_p2p = value != 0;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }

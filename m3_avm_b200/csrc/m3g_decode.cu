@@ -233,10 +233,15 @@ __global__ void __launch_bounds__(256) k_embed(const uint8_t* __restrict__ w, in
 // the largest logit) from the key the head GEMV's epilogue reduced with
 // atomicMax, and the step's bookkeeping; the key is cleared for the next step.
 __global__ void __launch_bounds__(32) k_pick_step(unsigned long long* key, int* pos, int* tokens, const int* nfixed,
-                                                  int max_pos, int* last) {
+                                                  int max_pos, int* last, int* step, const unsigned int* wait_cnt,
+                                                  unsigned int wait_mul, uint32_t* status) {
   grid_dep_wait();
   grid_dep_launch();
   if (threadIdx.x != 0) return;
+  if (wait_cnt) {  // sharded with peer stores: every rank's head CTAs have merged their keys
+    const unsigned int target = static_cast<unsigned int>(*step + 1) * wait_mul;
+    if (!wait_count_bounded(wait_cnt, target, 2000000000ull)) atomicOr(status, kStatusPeerTimeout);
+  }
   const unsigned long long k = *key;
   const int pick = k ? static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k)) : 0;  // 0: every logit NaN
   const int p = *pos, next = p + 1;
@@ -244,6 +249,7 @@ __global__ void __launch_bounds__(32) k_pick_step(unsigned long long* key, int* 
   if (next <= max_pos && next >= *nfixed) tokens[next] = pick;
   *pos = next;
   *key = 0ull;
+  *step += 1;
 }
 
 template <class Kern, class... Args>
@@ -317,6 +323,16 @@ struct m3g_decoder {
   float *rope = nullptr, *kc = nullptr, *vc = nullptr;
   int *dpos = nullptr, *tokens = nullptr, *nfixed = nullptr, *last = nullptr;
   unsigned long long* key = nullptr;  // greedy pick of the step (argmax epilogue of the head GEMV)
+  // One allocation holds what other ranks write into: hidden, the FFN
+  // activation, the greedy key, the arrival counters (2 per layer + head) and
+  // the step counter.  With peer stores its IPC mapping is opened by every rank.
+  uint8_t* xregion = nullptr;
+  size_t xregion_bytes = 0, off_hidden = 0, off_gub = 0, off_key = 0, off_cnt = 0;
+  unsigned int* cnt = nullptr;   // arrivals of every rank, per exchange: [layer][ffn, hidden], head
+  unsigned int* done = nullptr;  // this rank's finished CTAs, same slots
+  int* dstep = nullptr;          // steps completed (advanced by k_pick_step)
+  bool p2p = false;
+  uint8_t* peer_base[m3g::kMaxPeers] = {};
   int* h_io = nullptr;  // pinned: [0] token / nfixed staging, [1] last token
   uint32_t* status = nullptr;
   int pos = 0;           // host mirror of the device position
@@ -328,6 +344,12 @@ struct m3g_decoder {
 };
 
 namespace {
+
+// Rank p's copy of a region offset (this rank's own region for p == rank).
+template <class T>
+T* peer_at(const m3g_decoder* d, int p, size_t off) {
+  return reinterpret_cast<T*>(d->peer_base[p] + off);
+}
 
 int slot_shape(const m3g_decoder* d, int slot, int* in, int* out, bool* is_norm) {
   const int h = static_cast<int>(d->cfg.hidden), F = static_cast<int>(d->cfg.ffn);
@@ -455,6 +477,24 @@ int enqueue_step(m3g_decoder* d) {
   const int h = static_cast<int>(d->cfg.hidden), F = static_cast<int>(d->cfg.ffn);
   const int L = static_cast<int>(d->cfg.n_layers), V = static_cast<int>(d->cfg.vocab);
   const int mp = static_cast<int>(d->cfg.max_pos);
+  const bool pp = d->world > 1 && d->p2p;
+  // Exchange slots: 2l = silu(g)*u of layer l, 2l+1 = hidden after layer l, 2L = greedy key.
+  auto exchange = [&](int slot, size_t region_off, size_t elem_off, bool rows) {
+    m3g::PeerIO io;
+    io.npeer = d->world;
+    for (int p = 0; p < d->world; ++p) {
+      if (rows && p != d->rank) io.peer_y[p] = peer_at<float>(d, p, region_off) + elem_off;
+      io.peer_cnt[p] = peer_at<unsigned int>(d, p, d->off_cnt) + slot;
+    }
+    io.done_cnt = d->done + slot;
+    io.step = d->dstep;
+    return io;
+  };
+  auto wait_on = [&](m3g::PeerIO& io, int slot) {
+    io.wait_cnt = d->cnt + slot;
+    io.wait_mul = static_cast<unsigned int>(d->world);
+    io.step = d->dstep;
+  };
   const Tensor& E = d->t[kSlotEmbd];
   int be = 1, bb = 4;
   if (E.dtype == 1) bb = 2;
@@ -467,13 +507,23 @@ int enqueue_step(m3g_decoder* d) {
     const Tensor* T = &d->t[kSlotLayer0 + kPerLayer * l];
     const float* g_attn = reinterpret_cast<const float*>(T[kAttnNorm].d);
     const float* g_ffn = reinterpret_cast<const float*>(T[kFfnNorm].d);
+    // q|k|v reads hidden, which holds every rank's rows of the previous layer
+    m3g::PeerIO wq;
+    const m3g::PeerIO* pq = nullptr;
+    if (pp && l > 0) {
+      wait_on(wq, 2 * (l - 1) + 1);
+      pq = &wq;
+    }
+    auto gq = [&](const Gemv& g, float* y) {
+      return m3g::gemv_fused(d->device, g.dtype, g.w, g.len, d->hidden, nullptr, g_attn, nullptr, m3g::kXRmsNorm, y,
+                             g.in, g.out, d->st, true, nullptr, false, 0, pq);
+    };
     if (d->qkv[l].w) {
-      if (int rc = gemv(d, d->qkv[l], d->hidden, nullptr, g_attn, nullptr, m3g::kXRmsNorm, d->qkvb)) return rc;
+      if (int rc = gq(d->qkv[l], d->qkvb)) return rc;
     } else {
-      if (int rc = gemv(d, part(T[kQ]), d->hidden, nullptr, g_attn, nullptr, m3g::kXRmsNorm, d->qkvb)) return rc;
-      if (int rc = gemv(d, part(T[kK]), d->hidden, nullptr, g_attn, nullptr, m3g::kXRmsNorm, d->qkvb + h)) return rc;
-      if (int rc = gemv(d, part(T[kV]), d->hidden, nullptr, g_attn, nullptr, m3g::kXRmsNorm, d->qkvb + h + d->kvd))
-        return rc;
+      if (int rc = gq(part(T[kQ]), d->qkvb)) return rc;
+      if (int rc = gq(part(T[kK]), d->qkvb + h)) return rc;
+      if (int rc = gq(part(T[kV]), d->qkvb + h + d->kvd)) return rc;
     }
     m3g::AttnArgs a{};
     a.qkv = d->qkvb;
@@ -495,7 +545,21 @@ int enqueue_step(m3g_decoder* d) {
       DEC_CUDA(m3g::launch_pdl(m3g::k_attention<128>, agrid, dim3(m3g::kAttnThreads), attn_smem, d->st, a));
     }
     if (int rc = gemv(d, part(T[kO]), d->att, nullptr, nullptr, d->hidden, m3g::kXPlain, d->hidden)) return rc;
-    if (d->world > 1) {  // this rank's rows, then all-gathers of silu(g) * u and of hidden
+    if (pp) {  // this rank's rows, stored into every rank's buffers by the GEMV epilogues
+      float* hslot = d->gub + static_cast<size_t>(d->rank) * d->Fr;
+      const m3g::PeerIO gio = exchange(2 * l, d->off_gub, static_cast<size_t>(d->rank) * d->Fr, true);
+      const Gemv& gu = d->gu[l];
+      if (int rc = m3g::gemv_fused(d->device, gu.dtype, gu.w, gu.len, d->hidden, nullptr, g_ffn, nullptr,
+                                   m3g::kXRmsNorm, hslot, gu.in, gu.out, d->st, true, nullptr, true, 0, &gio))
+        return rc;
+      float* yslot = d->hidden + static_cast<size_t>(d->rank) * d->hr;
+      m3g::PeerIO dio = exchange(2 * l + 1, d->off_hidden, static_cast<size_t>(d->rank) * d->hr, true);
+      wait_on(dio, 2 * l);
+      const Tensor& Dn = T[kDown];
+      if (int rc = m3g::gemv_fused(d->device, Dn.dtype, Dn.d, Dn.len, d->gub, nullptr, nullptr, yslot, m3g::kXPlain,
+                                   yslot, Dn.in, Dn.out, d->st, true, nullptr, false, 0, &dio))
+        return rc;
+    } else if (d->world > 1) {  // this rank's rows, then NCCL all-gathers of silu(g) * u and of hidden
       float* hslot = d->gub + static_cast<size_t>(d->rank) * d->Fr;
       if (int rc = gemv(d, d->gu[l], d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, hslot, nullptr, true))
         return rc;
@@ -520,18 +584,29 @@ int enqueue_step(m3g_decoder* d) {
   }
   const float* g_out = reinterpret_cast<const float*>(d->t[kSlotOutNorm].d);
   const Tensor& H = d->t[kSlotOut];
-  if (H.out > 0) {  // the last rank of a small vocabulary may hold no rows
+  m3g::PeerIO hio;
+  const m3g::PeerIO* ph = nullptr;
+  if (pp) {  // the ranks' greedy keys merge into every rank's key
+    hio = exchange(2 * L, 0, 0, false);
+    for (int p = 0; p < d->world; ++p)
+      if (p != d->rank) hio.peer_key[p] = peer_at<unsigned long long>(d, p, d->off_key);
+    wait_on(hio, 2 * (L - 1) + 1);
+    ph = &hio;
+  }
+  if (H.out > 0) {  // the last rank of a small vocabulary may hold no rows (NCCL path only)
     if (int rc = m3g::gemv_fused(d->device, H.dtype, H.d, H.len, d->hidden, nullptr, g_out, nullptr, m3g::kXRmsNorm,
-                                 d->logits + H.row0, H.in, H.out, d->st, true, d->key, false, H.row0))
+                                 d->logits + H.row0, H.in, H.out, d->st, true, d->key, false, H.row0, ph))
       return rc;
   }
-  if (d->world > 1) {  // the greedy pick over all ranks' rows
+  if (d->world > 1 && !pp) {  // the greedy pick over all ranks' rows
     if (int rc = m3g::nccl_settle(d->comm, ncclAllReduce(d->key, d->key, 1, ncclUint64, ncclMax, d->comm, d->st),
                                   "ncclAllReduce(greedy key)", d->timeout_s))
       return rc;
   }
+  const unsigned int* pick_wait = pp ? d->cnt + 2 * L : nullptr;
   DEC_CUDA(m3g::launch_pdl(m3g::k_pick_step, dim3(1), dim3(32), 0, d->st, d->key, d->dpos, d->tokens,
-                           static_cast<const int*>(d->nfixed), mp, d->last));
+                           static_cast<const int*>(d->nfixed), mp, d->last, d->dstep, pick_wait,
+                           static_cast<unsigned int>(d->world), d->status));
   return M3G_OK;
 }
 
@@ -585,6 +660,77 @@ int check_status(m3g_decoder* d) {
     return host_fail(M3G_EINVAL, "decode step saw %s", (s & m3g::kStatusBadPos) ? "a position outside the KV cache"
                                                                              : "a token outside the vocabulary");
   }
+  return M3G_OK;
+}
+
+// Peer stores need every rank to map every other rank's exchange region
+// (CUDA IPC over NVLink).  The ranks swap handles with one all-gather and
+// agree (MIN all-reduce) on whether all mappings opened; otherwise every rank
+// keeps the NCCL all-gathers.
+int setup_peers(m3g_decoder* d) {
+  d->p2p = false;
+  d->peer_base[d->rank] = d->xregion;
+  if (d->world < 2 || d->world > m3g::kMaxPeers || !m3g::decode_p2p_enabled()) return M3G_OK;
+  if (static_cast<long long>(d->cfg.vocab) - static_cast<long long>(d->world - 1) * d->Vr < 1) return M3G_OK;
+  constexpr int kRec = 72;  // 64-byte handle + ok flag
+  uint8_t rec[kRec] = {};
+  cudaIpcMemHandle_t mine;
+  int ok = cudaIpcGetMemHandle(&mine, d->xregion) == cudaSuccess ? 1 : 0;
+  memcpy(rec, &mine, sizeof mine);
+  memcpy(rec + 64, &ok, sizeof ok);
+  uint8_t* dev = nullptr;
+  DEC_CUDA(cudaMalloc(&dev, static_cast<size_t>(kRec) * d->world + 16));
+  std::vector<uint8_t> all(static_cast<size_t>(kRec) * d->world);
+  int rc = M3G_OK;
+  cudaError_t e = cudaMemcpy(dev + kRec * d->rank, rec, kRec, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    rc = m3g::nccl_settle(d->comm, ncclAllGather(dev + kRec * d->rank, dev, kRec, ncclUint8, d->comm, d->st),
+                          "ncclAllGather(ipc handles)", d->timeout_s);
+    if (!rc) e = cudaStreamSynchronize(d->st);
+    if (!rc && e == cudaSuccess) e = cudaMemcpy(all.data(), dev, all.size(), cudaMemcpyDeviceToHost);
+  }
+  if (rc || e != cudaSuccess) {
+    cudaFree(dev);
+    return rc ? rc : host_fail(M3G_ECUDA, "peer handle exchange: %s", cudaGetErrorString(e));
+  }
+  int mine_ok = 1;
+  for (int p = 0; p < d->world; ++p) {
+    int okp = 0;
+    memcpy(&okp, all.data() + kRec * p + 64, sizeof okp);
+    if (!okp) mine_ok = 0;
+  }
+  for (int p = 0; p < d->world && mine_ok; ++p) {
+    if (p == d->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, all.data() + kRec * p, sizeof h);
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      mine_ok = 0;
+      break;
+    }
+    d->peer_base[p] = static_cast<uint8_t*>(ptr);
+  }
+  // agree: peer stores only if every rank mapped every peer
+  int* flag = reinterpret_cast<int*>(dev);
+  e = cudaMemcpy(flag, &mine_ok, sizeof mine_ok, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    rc = m3g::nccl_settle(d->comm, ncclAllReduce(flag, flag, 1, ncclInt, ncclMin, d->comm, d->st),
+                          "ncclAllReduce(peer agreement)", d->timeout_s);
+    if (!rc) e = cudaStreamSynchronize(d->st);
+  }
+  int all_ok = 0;
+  if (!rc && e == cudaSuccess) e = cudaMemcpy(&all_ok, flag, sizeof all_ok, cudaMemcpyDeviceToHost);
+  cudaFree(dev);
+  if (rc) return rc;
+  if (e != cudaSuccess) return host_fail(M3G_ECUDA, "peer agreement: %s", cudaGetErrorString(e));
+  if (!all_ok) {
+    for (int p = 0; p < d->world; ++p)
+      if (p != d->rank && d->peer_base[p]) cudaIpcCloseMemHandle(d->peer_base[p]);
+    for (int p = 0; p < d->world; ++p) d->peer_base[p] = p == d->rank ? d->xregion : nullptr;
+    return M3G_OK;
+  }
+  d->p2p = true;
   return M3G_OK;
 }
 
@@ -662,16 +808,29 @@ M3G_API int m3g_decoder_create_sharded(int device, const m3g_decoder_config* cfg
   const size_t h = c.hidden, F = c.ffn, mp = c.max_pos;
   if (int rc = m3g::status_word(device, &d->status)) return fail(rc);
   cudaError_t e = cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking);
-  if (e == cudaSuccess) e = cudaMalloc(&d->hidden, 4 * h);
+  auto up256 = [](size_t n) { return (n + 255) / 256 * 256; };
+  d->off_hidden = 0;
+  d->off_gub = up256(4 * h);
+  d->off_key = d->off_gub + up256(4 * 2 * F);
+  d->off_cnt = d->off_key + 256;
+  d->xregion_bytes = d->off_cnt + up256(4 * (2 * (2 * c.n_layers + 1) + 1));
+  if (e == cudaSuccess) e = cudaMalloc(&d->xregion, d->xregion_bytes);
+  if (e == cudaSuccess) e = cudaMemset(d->xregion, 0, d->xregion_bytes);
+  if (e == cudaSuccess) {
+    d->hidden = reinterpret_cast<float*>(d->xregion + d->off_hidden);
+    d->gub = reinterpret_cast<float*>(d->xregion + d->off_gub);
+    d->key = reinterpret_cast<unsigned long long*>(d->xregion + d->off_key);
+    d->cnt = reinterpret_cast<unsigned int*>(d->xregion + d->off_cnt);
+    d->done = d->cnt + (2 * c.n_layers + 1);
+    d->dstep = reinterpret_cast<int*>(d->done + (2 * c.n_layers + 1));
+  }
   if (e == cudaSuccess) e = cudaMalloc(&d->qkvb, 4 * (h + 2 * d->kvd));
   if (e == cudaSuccess) e = cudaMalloc(&d->att, 4 * h);
-  if (e == cudaSuccess) e = cudaMalloc(&d->gub, 4 * 2 * F);
   if (e == cudaSuccess) e = cudaMalloc(&d->logits, 4 * static_cast<size_t>(d->Vr) * world);
   if (e == cudaSuccess) e = cudaMalloc(&d->rope, 4 * mp * hd);
   if (e == cudaSuccess) e = cudaMalloc(&d->kc, 4 * c.n_layers * mp * d->kvd);
   if (e == cudaSuccess) e = cudaMalloc(&d->vc, 4 * c.n_layers * mp * d->kvd);
   if (e == cudaSuccess) e = cudaMalloc(&d->dpos, 4 * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&d->key, 16);
   if (e == cudaSuccess) e = cudaMalloc(&d->tokens, 4 * (mp + 1));
   if (e == cudaSuccess) e = cudaHostAlloc(&d->h_io, 4 * 4, cudaHostAllocDefault);
   if (e != cudaSuccess) {
@@ -692,7 +851,6 @@ M3G_API int m3g_decoder_create_sharded(int device, const m3g_decoder_config* cfg
     }
   e = cudaMemcpy(d->rope, rope.data(), 4 * mp * hd, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(d->dpos, 0, 4 * 4);
-  if (e == cudaSuccess) e = cudaMemset(d->key, 0, 16);
   if (e == cudaSuccess) e = cudaMemset(d->tokens, 0, 4 * (mp + 1));
   if (e == cudaSuccess) {
     const size_t attn_smem = sizeof(float) * (3 * hd + m3g::kAttnWarps * hd + 64 + mp);
@@ -704,6 +862,7 @@ M3G_API int m3g_decoder_create_sharded(int device, const m3g_decoder_config* cfg
   if (e != cudaSuccess) return fail(host_fail(M3G_ECUDA, "decoder setup: %s", cudaGetErrorString(e)));
   if (world > 1) {
     if (int rc = m3g::nccl_comm_create(rank, world, nccl_id128, d->timeout_s, &d->comm)) return fail(rc);
+    if (int rc = setup_peers(d)) return fail(rc);
   }
   *out = d;
   return M3G_OK;
@@ -840,6 +999,11 @@ M3G_API int m3g_decoder_truncate(m3g_decoder* d, uint64_t n) {
 
 M3G_API const float* m3g_decoder_logits_dev(const m3g_decoder* d) { return d ? d->logits : nullptr; }
 
+M3G_API int m3g_decoder_exchange(const m3g_decoder* d) {
+  if (!d) return -1;
+  return d->world == 1 ? 0 : (d->p2p ? 2 : 1);
+}
+
 M3G_API void* m3g_decoder_stream(const m3g_decoder* d) { return d ? static_cast<void*>(d->st) : nullptr; }
 
 M3G_API int m3g_decoder_set_graph(m3g_decoder* d, int use_graph) {
@@ -856,15 +1020,27 @@ M3G_API void m3g_decoder_destroy(m3g_decoder* d) {
   DevGuard g(d->device);
   if (d->st) cudaStreamSynchronize(d->st);
   drop_graph(d);  // the graph holds NCCL work: released before the communicator
+  if (d->comm && d->p2p) {
+    // no rank may still store into another's region when it is unmapped / freed
+    int* one = nullptr;
+    if (cudaMalloc(&one, 16) == cudaSuccess) {
+      m3g::nccl_settle(d->comm, ncclAllReduce(one, one, 1, ncclInt, ncclSum, d->comm, d->st), "ncclAllReduce(exit)",
+                       d->timeout_s);
+      cudaStreamSynchronize(d->st);
+      cudaFree(one);
+    }
+    for (int p = 0; p < d->world; ++p)
+      if (p != d->rank && d->peer_base[p]) cudaIpcCloseMemHandle(d->peer_base[p]);
+  }
   if (d->comm) m3g::nccl_comm_close(d->comm, d->timeout_s);
   d->comm = nullptr;
   for (Tensor& t : d->t)
     if (t.d) cudaFree(t.d);
   for (uint8_t* f : d->fused) cudaFree(f);
-  for (void* p : {static_cast<void*>(d->hidden), static_cast<void*>(d->qkvb), static_cast<void*>(d->att),
-                  static_cast<void*>(d->gub), static_cast<void*>(d->logits), static_cast<void*>(d->rope),
+  for (void* p : {static_cast<void*>(d->xregion), static_cast<void*>(d->qkvb), static_cast<void*>(d->att),
+                  static_cast<void*>(d->logits), static_cast<void*>(d->rope),
                   static_cast<void*>(d->kc), static_cast<void*>(d->vc), static_cast<void*>(d->dpos),
-                  static_cast<void*>(d->tokens), static_cast<void*>(d->key)})
+                  static_cast<void*>(d->tokens)})
     if (p) cudaFree(p);
   if (d->h_io) cudaFreeHost(d->h_io);
   if (d->st) cudaStreamDestroy(d->st);

@@ -124,6 +124,27 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// System-scope acquire load of a counter that other GPUs increment.
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until *cnt has reached target (wrap-safe), giving up after ~timeout_ns
+// of wall time or 2^24 polls.  Returns false when it gave up.
+__device__ __forceinline__ bool wait_count_bounded(const unsigned int* cnt, unsigned int target,
+                                                   uint64_t timeout_ns) {
+  if (static_cast<int>(ld_acquire_sys(cnt) - target) >= 0) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1; it < (1u << 24); ++it) {
+    __nanosleep(32);
+    if (static_cast<int>(ld_acquire_sys(cnt) - target) >= 0) return true;
+    if ((it & 63u) == 0u && global_ns() - t0 > timeout_ns) return false;
+  }
+  return false;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }

@@ -10,7 +10,10 @@ enum : uint32_t {
   kStatusCopyTimeout = 1u,  // a staged-copy wait gave up
   kStatusBadPos = 2u,       // a decode step found its position outside the KV cache
   kStatusBadToken = 4u,     // a decode step read a token id outside the vocabulary
+  kStatusPeerTimeout = 8u,  // a wait for other GPUs' rows gave up
 };
+
+constexpr int kMaxPeers = 8;  // ranks one decoder exchanges rows with (itself included)
 
 // Arguments of the staged streaming GEMV (k_gemv_stream).
 // Block = one producer warp + TS*RPI consumer threads.  Shared memory:
@@ -79,6 +82,33 @@ struct MmaArgs {
   int swiglu;
   // Row number the argmax key reports for local row 0 (a row shard's offset).
   long long key_row0;
+  // Row exchange between the GPUs of a sharded decode (FUSED only).  The
+  // epilogue also stores every output to the non-null peer_y[p] (this rank's
+  // slot in rank p's buffer).  Every CTA then adds 1 to the local done_cnt;
+  // the CTA that completes this step's count ((*step + 1) * gridDim.x) merges
+  // the local greedy key into the non-null peer_key[p] and adds 1 to every
+  // peer_cnt[p] (p < npeer, this rank included).  Before reading x, the
+  // consumers wait until *wait_cnt >= (*step + 1) * wait_mul.
+  float* peer_y[kMaxPeers];
+  unsigned long long* peer_key[kMaxPeers];
+  unsigned int* peer_cnt[kMaxPeers];
+  int npeer;
+  unsigned int* done_cnt;
+  const int* step;
+  const unsigned int* wait_cnt;
+  unsigned int wait_mul;
+};
+
+// Peer-exchange form of a decode GEMV (all pointers device-side; see MmaArgs).
+struct PeerIO {
+  float* peer_y[kMaxPeers] = {};
+  unsigned long long* peer_key[kMaxPeers] = {};
+  unsigned int* peer_cnt[kMaxPeers] = {};
+  int npeer = 0;
+  unsigned int* done_cnt = nullptr;
+  const int* step = nullptr;
+  const unsigned int* wait_cnt = nullptr;
+  unsigned int wait_mul = 0;
 };
 
 enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
@@ -91,13 +121,16 @@ enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
 int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, const float* x2,
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
                cudaStream_t st, bool decode, unsigned long long* argmax_key = nullptr, bool swiglu = false,
-               long long key_row0 = 0);
+               long long key_row0 = 0, const PeerIO* peers = nullptr, int* grid_out = nullptr);
 
 // GEMV with the greedy-pick epilogue, planned from the given device
 // attributes, reporting into the given status word (allocates nothing).
 int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, float* y, long long in_dim,
                    long long out_dim, cudaStream_t st, int sms, int smem_per_sm, int smem_optin, uint32_t* status,
                    unsigned long long* key);
+
+// Whether a sharded decoder may exchange rows by peer stores (tuning knob).
+bool decode_p2p_enabled();
 
 // The per-device status word the kernels set kStatus* bits in.
 int status_word(int device, uint32_t** out);

@@ -407,6 +407,23 @@ __device__ __forceinline__ void quantize_sb(const float (&v)[8], int sb, int lan
   if (lane == 0) sxs[sb] = amax > 0.f ? amax / 127.0f : 0.f;
 }
 
+// One CTA's arrival in a peer exchange (after its stores are fenced): the
+// CTA completing this step's count pushes the local greedy key to the peers
+// and signals each peer once.
+__device__ __forceinline__ void peer_arrive(const MmaArgs& a) {
+  const unsigned int target = static_cast<unsigned int>(*a.step + 1) * gridDim.x;
+  const unsigned int prev = atomicAdd(a.done_cnt, 1u);
+  if (prev + 1u != target) return;
+  __threadfence_system();
+  if (a.argmax_key) {
+    const unsigned long long k = atomicAdd(a.argmax_key, 0ull);
+    for (int p = 0; p < a.npeer; ++p)
+      if (a.peer_key[p] && k) atomicMax_system(a.peer_key[p], k);
+    __threadfence_system();
+  }
+  for (int p = 0; p < a.npeer; ++p) atomicAdd_system(a.peer_cnt[p], 1u);
+}
+
 // Named barriers of the kernel (0 is __syncthreads): 1..WK pair the warps of
 // two-tile stages (TPS > 1); the next id combines the norm's partial sums and
 // the one after releases the producer once x is loaded.  Ids stay low: the
@@ -434,7 +451,15 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
   const long long row0 = static_cast<long long>(blockIdx.x) * a.rows_per_cta;
   long long row_end = row0 + a.rows_per_cta;
   if (row_end > a.rows) row_end = a.rows;
-  if (row0 >= row_end) return;  // uniform across the CTA
+  if (row0 >= row_end) {  // uniform across the CTA; a peer-exchange CTA still counts
+    if constexpr (FUSED) {
+      if (a.npeer && threadIdx.x == 0) {
+        grid_dep_wait();
+        peer_arrive(a);
+      }
+    }
+    return;
+  }
   const int nrows = static_cast<int>(row_end - row0);
   const int ngroups = (nrows + SR - 1) / SR;
   const int nst = ngroups * a.NKC;
@@ -515,11 +540,18 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
             // Rows come in blocks of 8 gate rows then the 8 matching up rows
             // (every tile starts on a block boundary): h = silu(g) * u.
             const float u = __shfl_down_sync(0xFFFFFFFFu, acc, 8);
-            if ((lane & 15) < 8 && lane < rows_g)
-              a.y[(r >> 4) * 8 + (r & 7)] = __fmul_rn(__fdividef(acc, 1.0f + __expf(-acc)), u);
+            if ((lane & 15) < 8 && lane < rows_g) {
+              const long long o = (r >> 4) * 8 + (r & 7);
+              const float h = __fmul_rn(__fdividef(acc, 1.0f + __expf(-acc)), u);
+              a.y[o] = h;
+              for (int p = 0; p < a.npeer; ++p)
+                if (a.peer_y[p]) a.peer_y[p][o] = h;
+            }
           } else if (lane < rows_g) {
             const float yv = a.res ? a.res[r] + acc : acc;
             a.y[r] = yv;
+            for (int p = 0; p < a.npeer; ++p)
+              if (a.peer_y[p]) a.peer_y[p][r] = yv;
             if (a.argmax_key && yv == yv) best_key = max(best_key, argmax_key(yv, r + a.key_row0));
           }
         } else if (lane < rows_g) {
@@ -538,6 +570,11 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) best_key = max(best_key, __shfl_xor_sync(0xFFFFFFFFu, best_key, o));
         if (lane == 0 && best_key) atomicMax(a.argmax_key, best_key);
+      }
+      if (a.npeer) {  // this CTA's rows are in every peer's memory: count it
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0) peer_arrive(a);
       }
     }
     if (!ok && lane == 0) {
@@ -641,6 +678,13 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
       }
       grid_dep_wait();
       grid_dep_launch();
+      if (a.wait_cnt) {  // x holds other GPUs' rows: wait until every rank's CTAs have stored theirs
+        if (lane == 0) {
+          const unsigned int target = static_cast<unsigned int>(*a.step + 1) * a.wait_mul;
+          if (!wait_count_bounded(a.wait_cnt, target, kMmaTimeoutNs)) atomicOr(a.status, kStatusPeerTimeout);
+        }
+        __syncwarp();
+      }
       if (sbA >= 0) load8(a.x, sbA, xA);
       if (sbB >= 0) load8(a.x, sbB, xB);
       if (a.xmode == kXSiluMul) {
@@ -798,7 +842,7 @@ static cudaError_t launch_mma_cfg(const MmaArgs& a, int tps, int wk, int grid, s
 template <class F>
 static cudaError_t launch_mma_fmt(const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
                                   bool pdl) {
-  const bool fused = a.xmode != kXPlain || a.res || a.argmax_key || a.xfirst || a.swiglu;
+  const bool fused = a.xmode != kXPlain || a.res || a.argmax_key || a.xfirst || a.swiglu || a.npeer || a.wait_cnt;
   return fused ? launch_mma_cfg<F, true>(a, tps, wk, grid, smem, st, pdl)
                : launch_mma_cfg<F, false>(a, tps, wk, grid, smem, st, pdl);
 }

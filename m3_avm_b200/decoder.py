@@ -131,6 +131,11 @@ class GpuDecoder:
         return int(_lib.load().m3g_decoder_stream(self._h) or 0)
 
     @property
+    def exchange(self) -> str:
+        """'single', 'nccl' or 'peer-stores' (how a sharded engine moves rows)."""
+        return {0: "single", 1: "nccl", 2: "peer-stores"}.get(int(_lib.load().m3g_decoder_exchange(self._h)), "?")
+
+    @property
     def logits_ptr(self) -> int:
         return int(_lib.load().m3g_decoder_logits_dev(self._h) or 0)
 
