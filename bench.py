@@ -244,6 +244,59 @@ def decode_leg(args, dev, world: int = 1) -> dict:
     return out
 
 
+BATCHED_IN, BATCHED_OUT, BATCHED_B = 8192, 28672, (1, 4, 16, 32, 64)
+
+
+def batched_leg(args, dev) -> dict:
+    """Batched decode GEMM: Q4_K 28672 x 8192 weights against X of B x 8192,
+    B in {1, 4, 16, 32, 64}; rotating resident weight copies (> 3x L2), CUDA
+    events around CUDA-graph replays.  Effective GB/s counts the weights once
+    plus X and Y (4*B*in + 4*B*out); TFLOP/s counts 2*B*in*out."""
+    import torch
+
+    from m3_avm_b200 import _lib, synth
+    from m3_avm_b200.inference_gpu import GpuOffload
+
+    raw = synth.weights(DTYPE, BATCHED_IN, BATCHED_OUT, seed=5)
+    props = torch.cuda.get_device_properties(dev)
+    l2 = getattr(props, "L2_cache_size", 126 * 1024 * 1024) or 126 * 1024 * 1024
+    n_copies = max(2, math.ceil(3 * l2 / raw.size))
+    g = GpuOffload.try_new(BATCHED_IN, BATCHED_OUT, device=dev.index or 0)
+    for c in range(n_copies):
+        if not g.upload(c, DTYPE, raw, BATCHED_IN, BATCHED_OUT):
+            raise RuntimeError("upload failed: " + _lib.last_error())
+    out = {"workload": f"q4k_batched_{BATCHED_OUT}x{BATCHED_IN}", "weight_copies": n_copies, "sweep": {}}
+    peaks, kind = measured_peaks()
+    for B in BATCHED_B:
+        X = torch.from_numpy(synth.activations(BATCHED_IN, seed=6, batch=B)).to(dev)
+        Y = torch.empty((B, BATCHED_OUT), dtype=torch.float32, device=dev)
+        cap = torch.cuda.Stream(dev)
+        reps = max(3, min(60, int(2000 / B)))
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=cap, capture_error_mode="thread_local"):
+            for c in range(n_copies):
+                g.matvec_dev(c, X, Y, stream=cap.cuda_stream)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1e3 / (reps * n_copies)
+        abytes = algorithmic_bytes(BATCHED_IN, BATCHED_OUT, DTYPE, batch=B)
+        flops = 2.0 * B * BATCHED_IN * BATCHED_OUT
+        out["sweep"][str(B)] = {"us": round(us, 2), "gbs": round(abytes / us / 1e3, 1),
+                                "tflops": round(flops / us / 1e6, 2),
+                                "frac_of_hbm": round(abytes / us / 1e3 / float(peaks["hbm_gbs"]), 4)}
+        del gr
+    g.close()
+    out["kernel"] = "k_xprep8 + k_gemm8_q4k (8 columns per pass, mma.sync int8); B=1 takes k_gemv_mma"
+    return out
+
+
 def cpu_decode_rate(shape, tensors, prompt, n_tokens: int = 3) -> dict:
     """The oracle's restatement of forward_one (reference CPU path) on the host cores."""
     from oracle import oracle as O
@@ -444,6 +497,9 @@ def run_ours(args) -> int:
     decode = None
     if not args.no_decode:
         decode = decode_leg(args, dev, world)
+    batched = None
+    if world == 1 and not args.no_batched:
+        batched = batched_leg(args, dev)
 
     if rank == 0:
         line = {
@@ -467,6 +523,7 @@ def run_ours(args) -> int:
             "clocks": clocks,
             "device_status": status,
             "decode": decode,
+            "batched": batched,
         }
         print(json.dumps(line), flush=True)
     g.close()
@@ -574,6 +631,7 @@ def main() -> int:
     ap.add_argument("--no-graph", action="store_true", help="launch each step from the host instead of a CUDA graph")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the 1B decode tokens/s leg")
+    ap.add_argument("--no-batched", action="store_true", help="skip the batched Q4_K 28672x8192 sweep")
     ap.add_argument("--workload", choices=["gemv", "lmhead"], default="gemv",
                     help="gemv: Q4_K 14336x4096 GEMV per GPU (the headline); "
                          "lmhead: Q6_K 128256x4096 rows sharded over the GPUs + all-gather")

@@ -92,6 +92,7 @@ struct Tuning {
   int64_t mma_xfirst = 0;         // issue the ring past PRE only once x is loaded
   int64_t decode_xfirst = 0;      // the same for the GEMVs of a decode step
   int64_t decode_p2p = 1;         // sharded decode: peer stores over NVLink instead of NCCL all-gathers
+  int64_t gemm8 = 1;              // batched Q4_K: 8 columns per launch (k_gemm8_q4k) instead of one GEMV each
 };
 Tuning g_tune;
 
@@ -323,8 +324,75 @@ int gemv_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const fl
   return M3G_OK;
 }
 
+struct Gemm8Plan {
+  m3g::Gemm8Args a{};
+  int grid = 0;
+  size_t smem = 0;
+};
+
+// Batched Q4_K: chunks of KC <= 8 super-blocks (one prepared-x record each,
+// double-buffered), 16-row weight stages of one chunk, per-(row, column) sums.
+bool plan_gemm8(const FmtInfo& f, long long in_dim, long long rows, const uint8_t* w, const float* x,
+                const DevState& ds, Gemm8Plan& p) {
+  if (f.fmt != 12 || in_dim % 256) return false;
+  if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16) return false;
+  if (rows > (1ll << 31) - 1 || in_dim > (1 << 20)) return false;
+  const long long NSB = in_dim / 256;
+  const long long KC = std::min<long long>(8, NSB);
+  const long long NKC = (NSB + KC - 1) / KC;
+  long long GS = (KC * 144 + 15) / 16 * 16;
+  while (GS % 128 != 32) GS += 16;
+  const long long rpc = std::max<long long>(1, (rows + ds.sms - 1) / ds.sms);
+  const long long xc = KC * m3g::kGemm8RecBytes;
+  const long long off_stage = (2 * xc + 127) / 128 * 128;
+  const long long per_stage = 16 * GS + 16 * 8 * 8 * 4;
+  const long long acc = (rpc * 8 * 4 + 15) / 16 * 16;
+  long long NS = std::min<long long>(4, (ds.smem_optin - off_stage - acc - 256) / per_stage);
+  if (NS < 2) return false;
+  p.a.rows = static_cast<int>(rows);
+  p.a.RB = static_cast<int>(NSB * 144);
+  p.a.NSB = static_cast<int>(NSB);
+  p.a.KC = static_cast<int>(KC);
+  p.a.NKC = static_cast<int>(NKC);
+  p.a.NS = static_cast<int>(NS);
+  p.a.GS = static_cast<int>(GS);
+  p.a.rows_per_cta = static_cast<int>(rpc);
+  p.a.off_stage = static_cast<int>(off_stage);
+  p.a.off_red = static_cast<int>(off_stage + NS * 16 * GS);
+  p.a.off_acc = static_cast<int>(p.a.off_red + NS * 16 * 8 * 8 * 4);
+  p.a.off_bar = static_cast<int>(p.a.off_acc + acc);
+  p.smem = static_cast<size_t>(p.a.off_bar + (2 * NS + 4) * 8 + 16);
+  p.grid = static_cast<int>((rows + rpc - 1) / rpc);
+  return static_cast<long long>(p.smem) <= ds.smem_optin;
+}
+
 int gemv_batch_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const float* x, float* y,
                       long long in_dim, long long out_dim, long long batch, cudaStream_t st) {
+  Gemm8Plan gp;
+  if (batch >= 2 && !g_tune.force_generic && g_tune.mma && g_tune.gemm8 && plan_gemm8(f, in_dim, out_dim, w, x, ds, gp)) {
+    // X is quantised once per pass of 8 columns into a stream-ordered workspace.
+    uint8_t* ws = nullptr;
+    const size_t ws_bytes = static_cast<size_t>(gp.a.NSB) * m3g::kGemm8RecBytes;
+    M3G_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), ws_bytes, st));
+    int rc = M3G_OK;
+    for (long long p0 = 0; p0 < batch && rc == M3G_OK; p0 += m3g::kGemm8Cols) {
+      const int cols = static_cast<int>(std::min<long long>(m3g::kGemm8Cols, batch - p0));
+      cudaError_t e = m3g::launch_xprep8(x + p0 * in_dim, cols, static_cast<int>(in_dim), ws, st);
+      if (e == cudaSuccess) {
+        gp.a.w = w;
+        gp.a.xq = ws;
+        gp.a.y = y + p0 * out_dim;
+        gp.a.status = ds.status;
+        gp.a.cols = cols;
+        gp.a.ldy = static_cast<int>(out_dim);
+        e = m3g::launch_gemm8_q4k(gp.a, gp.grid, gp.smem, st);
+      }
+      if (e != cudaSuccess) rc = cuda_fail(e, "batched GEMV launch");
+      else g_launches.fetch_add(2, std::memory_order_relaxed);
+    }
+    cudaFreeAsync(ws, st);
+    return rc;
+  }
   for (long long b = 0; b < batch; ++b) {
     int rc = gemv_launch(ds, f, w, x + b * in_dim, y + b * out_dim, in_dim, out_dim, st);
     if (rc) return rc;
@@ -528,6 +596,7 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "mma_xfirst")) g_tune.mma_xfirst = value != 0;
   else if (!strcmp(key, "decode_xfirst")) g_tune.decode_xfirst = value != 0;
   else if (!strcmp(key, "decode_p2p")) g_tune.decode_p2p = value != 0;
+  else if (!strcmp(key, "gemm8")) g_tune.gemm8 = value != 0;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }

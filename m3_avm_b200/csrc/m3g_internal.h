@@ -135,6 +135,20 @@ bool decode_p2p_enabled();
 // The per-device status word the kernels set kStatus* bits in.
 int status_word(int device, uint32_t** out);
 
+// Batched Q4_K GEMV, up to 8 columns of X per launch (m3g_mma.cu).
+constexpr int kGemm8Cols = 8;
+constexpr int kGemm8RecBytes = 6432;  // prepared-x bytes per 256-element super-block
+struct Gemm8Args {
+  const uint8_t* w;
+  const uint8_t* xq;
+  float* y;
+  uint32_t* status;
+  int rows, RB, NSB, KC, NKC, NS, GS, rows_per_cta, cols, ldy;
+  int off_stage, off_red, off_acc, off_bar;
+};
+cudaError_t launch_xprep8(const float* x, int cols, int in_dim, uint8_t* out, cudaStream_t st);
+cudaError_t launch_gemm8_q4k(const Gemm8Args& a, int grid, size_t smem, cudaStream_t st);
+
 int mma_sb_bytes(int fmt);
 cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
                             bool pdl);

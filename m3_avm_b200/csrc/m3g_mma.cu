@@ -858,4 +858,327 @@ cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int tps, int wk, int grid
   }
 }
 
+// ================================================================ batched GEMV, 8 columns per pass
+//
+// Y[b][r] = sum_k X[b][k] W[r][k] for up to 8 rows of X per launch (Q4_K).
+// k_xprep8 quantises X once into one record per 256-element super-block: the
+// three int8 slices of every column (the B = 1 kernel's representation), the
+// 32-element group sums and the column scales.  k_gemm8_q4k walks the K
+// chunks outermost: one TMA bulk copy brings a chunk's records into shared
+// memory for all of the CTA's row tiles, the 8 consumer warps each take one
+// super-block of the staged 16-row tile and run three m16n8k32 MMAs per
+// sub-block (one per slice) with the 8 columns as N, and the producer adds
+// the warps' partials into per-(row, column) sums in shared memory, writing Y
+// after the last chunk.  Same integer math and fp32 epilogue as k_gemv_mma.
+constexpr int kXB = 8;                                 // columns per pass
+constexpr int kXRecSlices = 8 * 3 * kXB * 32;          // [sub-block j][slice][column][32]
+constexpr int kXRecSum = kXRecSlices;                  // f32 [j][column]
+constexpr int kXRecScale = kXRecSum + 8 * kXB * 4;     // f32 [column]
+constexpr int kXRec = kXRecScale + kXB * 4;            // 6432 bytes per super-block
+
+__global__ void __launch_bounds__(256) k_xprep8(const float* __restrict__ x, int cols, int in_dim,
+                                                uint8_t* __restrict__ out) {
+  const int sb = blockIdx.x, b = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (b < cols) {
+    const float4* p4 = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * in_dim + 256 * sb + 8 * lane);
+    const float4 v0 = __ldg(p4), v1 = __ldg(p4 + 1);
+    v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
+    v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+  uint32_t s0[2] = {0u, 0u}, s1[2] = {0u, 0u}, s2[2] = {0u, 0u};
+  float part = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    part += v[i];
+    const float q = v[i] * inv;
+    const float q0 = rintf(q);
+    const float u1 = (q - q0) * 254.0f;
+    const float q1 = rintf(u1);
+    const float q2 = rintf((u1 - q1) * 254.0f);
+    const int sh = 8 * (i & 3);
+    s0[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q0)) & 0xFFu) << sh;
+    s1[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q1)) & 0xFFu) << sh;
+    s2[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q2)) & 0xFFu) << sh;
+  }
+  uint8_t* rec = out + static_cast<size_t>(sb) * kXRec;
+  const int j = lane >> 2;
+  uint8_t* dst = rec + ((j * 3) * kXB + b) * 32 + 8 * (lane & 3);
+  *reinterpret_cast<uint2*>(dst) = make_uint2(s0[0], s0[1]);
+  *reinterpret_cast<uint2*>(dst + kXB * 32) = make_uint2(s1[0], s1[1]);
+  *reinterpret_cast<uint2*>(dst + 2 * kXB * 32) = make_uint2(s2[0], s2[1]);
+  float p32 = part + __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+  p32 += __shfl_xor_sync(0xFFFFFFFFu, p32, 2);
+  if ((lane & 3) == 0) reinterpret_cast<float*>(rec + kXRecSum)[j * kXB + b] = p32;
+  if (lane == 0) reinterpret_cast<float*>(rec + kXRecScale)[b] = amax > 0.f ? amax / 127.0f : 0.f;
+}
+
+static_assert(kXRec == kGemm8RecBytes, "prepared-x record size");
+static_assert(kXB == kGemm8Cols, "columns per pass");
+
+// x operands of one super-block for the thread (g, t): B fragments of the 8
+// sub-blocks x 3 slices for column g, and the sums / scales of its
+// accumulator columns 2t and 2t+1.
+struct XB8 {
+  uint2 b[8][3];
+  float2 sum[8];
+  float2 sx;  // column scales / 16
+};
+
+__device__ __forceinline__ void load_xb8(const uint8_t* rec, int g, int t, XB8& o) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int s = 0; s < 3; ++s) o.b[j][s] = lds64(rec + ((j * 3 + s) * kXB + g) * 32 + 8 * t);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o.sum[j] = *reinterpret_cast<const float2*>(rec + kXRecSum + (j * kXB + 2 * t) * 4);
+  const float2 sc = *reinterpret_cast<const float2*>(rec + kXRecScale + 2 * t * 4);
+  o.sx = make_float2(sc.x * (1.0f / 16.0f), sc.y * (1.0f / 16.0f));
+}
+
+// One 16-row Q4_K super-block tile against 8 columns: v[0], v[1] = rows g
+// and columns 2t, 2t+1; v[2], v[3] = row g + 8.
+__device__ __forceinline__ void tile8_q4k(const uint8_t* sm, uint32_t rg, uint32_t rg8, const XB8& xb, int t,
+                                          float (&v)[4]) {
+  const uint4 hg = lds128(sm, rg);
+  const uint4 hg8 = lds128(sm, rg8);
+  const uint32_t qo = rg + 16 + 8 * t, qo8 = rg8 + 16 + 8 * t;
+  uint32_t scl, sch, ml, mh, scl8, sch8, ml8, mh8;
+  MmaQ4K::sc_words(hg, scl, sch, ml, mh);
+  MmaQ4K::sc_words(hg8, scl8, sch8, ml8, mh8);
+  int alo[3][4], ahi[3][4];
+#pragma unroll
+  for (int s = 0; s < 3; ++s)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) alo[s][i] = ahi[s][i] = 0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint2 q = lds64(sm, qo + 32 * c);
+    const uint2 q8 = lds64(sm, qo8 + 32 * c);
+    const uint32_t w = c < 2 ? scl : sch, w8 = c < 2 ? scl8 : sch8;
+    int sa, sb, sa8, sb8;
+    if (c & 1) {
+      sa = ubyte<2>(w); sb = ubyte<3>(w); sa8 = ubyte<2>(w8); sb8 = ubyte<3>(w8);
+    } else {
+      sa = ubyte<0>(w); sb = ubyte<1>(w); sa8 = ubyte<0>(w8); sb8 = ubyte<1>(w8);
+    }
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      int dlo[4], dhi[4];
+      mma_k32_u8s8(q.x & 0x0F0F0F0Fu, q8.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, q8.y & 0x0F0F0F0Fu,
+                   xb.b[2 * c][s].x, xb.b[2 * c][s].y, dlo);
+      mma_k32_u8s8(q.x & 0xF0F0F0F0u, q8.x & 0xF0F0F0F0u, q.y & 0xF0F0F0F0u, q8.y & 0xF0F0F0F0u,
+                   xb.b[2 * c + 1][s].x, xb.b[2 * c + 1][s].y, dhi);
+      alo[s][0] += sa * dlo[0];
+      alo[s][1] += sa * dlo[1];
+      alo[s][2] += sa8 * dlo[2];
+      alo[s][3] += sa8 * dlo[3];
+      ahi[s][0] += sb * dhi[0];
+      ahi[s][1] += sb * dhi[1];
+      ahi[s][2] += sb8 * dhi[2];
+      ahi[s][3] += sb8 * dhi[3];
+    }
+  }
+  const float d = f16_to_f32(hg.x), dmin = f16_to_f32(hg.x >> 16);
+  const float d8 = f16_to_f32(hg8.x), dmin8 = f16_to_f32(hg8.x >> 16);
+  // min term dmin * sum_j m_j * sum(x_j), per row and column
+  float mg[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t mw = j < 4 ? ml : mh, mw8 = j < 4 ? ml8 : mh8;
+    const int k = j & 3;
+    const float m = static_cast<float>((mw >> (8 * k)) & 0xFFu);
+    const float m8 = static_cast<float>((mw8 >> (8 * k)) & 0xFFu);
+    mg[0] = fmaf(m, xb.sum[j].x, mg[0]);
+    mg[1] = fmaf(m, xb.sum[j].y, mg[1]);
+    mg[2] = fmaf(m8, xb.sum[j].x, mg[2]);
+    mg[3] = fmaf(m8, xb.sum[j].y, mg[3]);
+  }
+  float main[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    main[i] = static_cast<float>(16 * alo[0][i] + ahi[0][i]) +
+              static_cast<float>(16 * alo[1][i] + ahi[1][i]) * (1.0f / 254.0f) +
+              static_cast<float>(16 * alo[2][i] + ahi[2][i]) * (1.0f / 64516.0f);
+  v[0] = fmaf(d * xb.sx.x, main[0], -dmin * mg[0]);
+  v[1] = fmaf(d * xb.sx.y, main[1], -dmin * mg[1]);
+  v[2] = fmaf(d8 * xb.sx.x, main[2], -dmin8 * mg[2]);
+  v[3] = fmaf(d8 * xb.sx.y, main[3], -dmin8 * mg[3]);
+}
+
+__global__ void __launch_bounds__(288, 1) k_gemm8_q4k(const Gemm8Args a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long row0 = static_cast<long long>(blockIdx.x) * a.rows_per_cta;
+  long long row_end = row0 + a.rows_per_cta;
+  if (row_end > a.rows) row_end = a.rows;
+  if (row0 >= row_end) return;  // uniform across the CTA
+  const int nrows = static_cast<int>(row_end - row0);
+  const int ngroups = (nrows + 15) / 16;
+  const int nst = ngroups * a.NKC;  // stage s = (chunk s / ngroups, row group s % ngroups)
+  const uint32_t XC = static_cast<uint32_t>(a.KC) * kXRec;
+  const uint32_t stage_bytes = 16u * static_cast<uint32_t>(a.GS);
+  float* red = reinterpret_cast<float*>(smem + a.off_red);  // [NS][16 rows][8 columns][8 warps]
+  float* acc = reinterpret_cast<float*>(smem + a.off_acc);  // [nrows][8]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+  uint64_t* empty = full + a.NS;
+  uint64_t* xfull = empty + a.NS;
+  uint64_t* xempty = xfull + 2;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(xempty + 2);
+  if (tid == 0) {
+    for (int s = 0; s < a.NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], 8);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  for (int i = tid; i < nrows * kXB; i += blockDim.x) acc[i] = 0.f;
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------ producer warp
+    uint64_t policy = 0;
+    if (lane == 0) policy = l2_evict_first_policy();
+    policy = __shfl_sync(0xFFFFFFFFu, policy, 0);
+    auto issue_x = [&](int kc) {
+      const int nsb = min(a.KC, a.NSB - kc * a.KC);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&xfull[kc & 1], static_cast<uint32_t>(nsb * kXRec));
+        bulk_g2s(smem + (kc & 1) * XC, a.xq + static_cast<size_t>(kc) * a.KC * kXRec,
+                 static_cast<uint32_t>(nsb * kXRec), &xfull[kc & 1], 0ull);
+      }
+      __syncwarp();
+    };
+    auto issue = [&](int s) {
+      const int kc = s / ngroups, grp = s - kc * ngroups;
+      const int rows_g = min(16, nrows - 16 * grp);
+      const int seg = min(a.KC, a.NSB - kc * a.KC) * MmaQ4K::kSBBytes;
+      const int b = s % a.NS;
+      if (lane == 0) mbar_arrive_expect_tx(&full[b], static_cast<uint32_t>(rows_g * seg));
+      __syncwarp();
+      if (lane < rows_g) {
+        const long long row = row0 + 16 * grp + lane;
+        bulk_g2s(smem + a.off_stage + b * stage_bytes + static_cast<size_t>(lane) * a.GS,
+                 a.w + row * a.RB + static_cast<long long>(kc) * a.KC * MmaQ4K::kSBBytes, static_cast<uint32_t>(seg),
+                 &full[b], policy);
+      }
+    };
+    issue_x(0);
+    if (a.NKC > 1) issue_x(1);
+    for (int s = 0; s < min(a.NS, nst); ++s) issue(s);
+    int buf = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int s = 0; s < nst && ok; ++s) {
+      ok = mbar_wait_bounded(&empty[buf], ph, kMmaTimeoutNs, abort_flag);
+      if (!ok) break;
+      const int kc = s / ngroups, grp = s - kc * ngroups;
+      const int rows_g = min(16, nrows - 16 * grp);
+      const float* rb = red + static_cast<size_t>(buf) * 16 * kXB * 8;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int idx = lane + 32 * q, r = idx >> 3, b = idx & 7;
+        if (r < rows_g) {
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) v += rb[idx * 8 + w];
+          const int ar = (16 * grp + r) * kXB + b;
+          const float tot = acc[ar] + v;
+          acc[ar] = tot;
+          if (kc == a.NKC - 1 && b < a.cols) a.y[static_cast<long long>(b) * a.ldy + row0 + 16 * grp + r] = tot;
+        }
+      }
+      __syncwarp();
+      if (s + a.NS < nst) {
+        if (lane == 0) fence_proxy_async_smem();
+        issue(s + a.NS);
+      }
+      if (grp == ngroups - 1 && kc + 2 < a.NKC) {  // chunk kc fully consumed: its buffer takes chunk kc + 2
+        ok = mbar_wait_bounded(&xempty[kc & 1], (kc >> 1) & 1, kMmaTimeoutNs, abort_flag);
+        if (!ok) break;
+        if (lane == 0) fence_proxy_async_smem();
+        issue_x(kc + 2);
+      }
+      if (++buf == a.NS) { buf = 0; ph ^= 1u; }
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      atomicOr(a.status, kStatusCopyTimeout);
+      for (int s = 0; s < a.NS; ++s) (void)mbar_wait_bounded(&full[s], 0u, kMmaTimeoutNs / 8);
+      for (int i = 0; i < 2; ++i) (void)mbar_wait_bounded(&xfull[i], 0u, kMmaTimeoutNs / 8);
+    }
+    return;
+  }
+
+  // -------------------------------------------------- consumer warps
+  const int cw = warp - 1;  // super-block cw of every staged chunk
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t off_g = static_cast<uint32_t>(g * a.GS + cw * MmaQ4K::kSBBytes);
+  const uint32_t off_g8 = static_cast<uint32_t>((g + 8) * a.GS + cw * MmaQ4K::kSBBytes);
+  XB8 xb;
+  int buf = 0, loaded_kc = -1;
+  uint32_t ph = 0;
+  bool active = false;
+  for (int s = 0; s < nst; ++s) {
+    const int kc = s / ngroups, grp = s - kc * ngroups;
+    if (kc != loaded_kc) {
+      if (loaded_kc >= 0) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xempty[loaded_kc & 1]);
+      }
+      if (!mbar_wait_bounded(&xfull[kc & 1], (kc >> 1) & 1, kMmaTimeoutNs, abort_flag)) {
+        if (lane == 0) {
+          *abort_flag = 1;
+          atomicOr(a.status, kStatusCopyTimeout);
+        }
+        return;
+      }
+      active = cw < min(a.KC, a.NSB - kc * a.KC);
+      if (active) load_xb8(smem + (kc & 1) * XC + cw * kXRec, g, t, xb);
+      loaded_kc = kc;
+    }
+    if (!mbar_wait_bounded(&full[buf], ph, kMmaTimeoutNs, abort_flag)) {
+      if (lane == 0) {
+        *abort_flag = 1;
+        atomicOr(a.status, kStatusCopyTimeout);
+      }
+      return;
+    }
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t st = static_cast<uint32_t>(a.off_stage) + static_cast<uint32_t>(buf) * stage_bytes;
+    if (active) tile8_q4k(smem, st + off_g, st + off_g8, xb, t, v);
+    float* rb = red + static_cast<size_t>(buf) * 16 * kXB * 8;
+    rb[(g * kXB + 2 * t) * 8 + cw] = v[0];
+    rb[(g * kXB + 2 * t + 1) * 8 + cw] = v[1];
+    rb[((g + 8) * kXB + 2 * t) * 8 + cw] = v[2];
+    rb[((g + 8) * kXB + 2 * t + 1) * 8 + cw] = v[3];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[buf]);
+    if (++buf == a.NS) { buf = 0; ph ^= 1u; }
+  }
+}
+
+cudaError_t launch_xprep8(const float* x, int cols, int in_dim, uint8_t* out, cudaStream_t st) {
+  k_xprep8<<<in_dim / 256, 256, 0, st>>>(x, cols, in_dim, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm8_q4k(const Gemm8Args& a, int grid, size_t smem, cudaStream_t st) {
+  cudaError_t e = set_smem_once<k_gemm8_q4k>(smem);
+  if (e != cudaSuccess) return e;
+  k_gemm8_q4k<<<grid, 288, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace m3g

@@ -255,3 +255,19 @@ def test_decoder_failure_rules(torch_cuda):
     with pytest.raises(_lib.M3GError):
         GpuDecoder(model.LlamaShape(n_heads=24))  # head_dim 2048 / 24 is not whole
     d.close()
+
+
+def test_decoder_from_gguf_file_equals_direct_upload(torch_cuda, tmp_path):
+    from m3_avm_b200 import gguf as G
+
+    p = str(tmp_path / "well.gguf")
+    G.write_synthetic_model(p, WELL, seed=51)
+    dec, shape = G.load_decoder(p, max_pos=16)
+    assert shape == WELL
+    direct = gpu_decoder(WELL, model.synthetic_tensors(WELL, 51), 16)
+    for t in (3, 999, 4095):
+        a = dec.forward_one(t)
+        b = direct.forward_one(t)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    dec.close()
+    direct.close()
