@@ -330,24 +330,29 @@ struct Gemm8Plan {
   size_t smem = 0;
 };
 
-// Batched Q4_K: chunks of KC <= 8 super-blocks (one prepared-x record each,
-// double-buffered), 16-row weight stages of one chunk, per-(row, column) sums.
+// Batched Q4_K: chunks of KC <= 4 super-blocks (one prepared-x record each,
+// double-buffered), stages of 8 / KC row tiles of one chunk, per-(row,
+// column) sums; sized so two CTAs share an SM.
 bool plan_gemm8(const FmtInfo& f, long long in_dim, long long rows, const uint8_t* w, const float* x,
                 const DevState& ds, Gemm8Plan& p) {
   if (f.fmt != 12 || in_dim % 256) return false;
   if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16) return false;
   if (rows > (1ll << 31) - 1 || in_dim > (1 << 20)) return false;
   const long long NSB = in_dim / 256;
-  const long long KC = std::min<long long>(8, NSB);
+  long long KC = 4;
+  while (KC > NSB) KC /= 2;  // 4, 2 or 1 super-blocks per chunk (8 / KC row tiles per stage)
   const long long NKC = (NSB + KC - 1) / KC;
+  const long long SR = 16 * (8 / KC);
   long long GS = (KC * 144 + 15) / 16 * 16;
   while (GS % 128 != 32) GS += 16;
-  const long long rpc = std::max<long long>(1, (rows + ds.sms - 1) / ds.sms);
+  const long long ctas = 2ll * ds.sms;
+  const long long rpc = std::max<long long>(1, (rows + ctas - 1) / ctas);
   const long long xc = KC * m3g::kGemm8RecBytes;
   const long long off_stage = (2 * xc + 127) / 128 * 128;
-  const long long per_stage = 16 * GS + 16 * 8 * 8 * 4;
+  const long long per_stage = SR * GS + SR * 8 * KC * 4;
   const long long acc = (rpc * 8 * 4 + 15) / 16 * 16;
-  long long NS = std::min<long long>(4, (ds.smem_optin - off_stage - acc - 256) / per_stage);
+  const long long budget = std::min<long long>(ds.smem_optin, ds.smem_per_sm / 2 - 1024);
+  long long NS = std::min<long long>(4, (budget - off_stage - acc - 256) / per_stage);
   if (NS < 2) return false;
   p.a.rows = static_cast<int>(rows);
   p.a.RB = static_cast<int>(NSB * 144);
@@ -358,12 +363,12 @@ bool plan_gemm8(const FmtInfo& f, long long in_dim, long long rows, const uint8_
   p.a.GS = static_cast<int>(GS);
   p.a.rows_per_cta = static_cast<int>(rpc);
   p.a.off_stage = static_cast<int>(off_stage);
-  p.a.off_red = static_cast<int>(off_stage + NS * 16 * GS);
-  p.a.off_acc = static_cast<int>(p.a.off_red + NS * 16 * 8 * 8 * 4);
+  p.a.off_red = static_cast<int>(off_stage + NS * SR * GS);
+  p.a.off_acc = static_cast<int>(p.a.off_red + NS * SR * 8 * KC * 4);
   p.a.off_bar = static_cast<int>(p.a.off_acc + acc);
   p.smem = static_cast<size_t>(p.a.off_bar + (2 * NS + 4) * 8 + 16);
   p.grid = static_cast<int>((rows + rpc - 1) / rpc);
-  return static_cast<long long>(p.smem) <= ds.smem_optin;
+  return static_cast<long long>(p.smem) <= budget;
 }
 
 int gemv_batch_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const float* x, float* y,

@@ -922,36 +922,18 @@ __global__ void __launch_bounds__(256) k_xprep8(const float* __restrict__ x, int
 static_assert(kXRec == kGemm8RecBytes, "prepared-x record size");
 static_assert(kXB == kGemm8Cols, "columns per pass");
 
-// x operands of one super-block for the thread (g, t): B fragments of the 8
-// sub-blocks x 3 slices for column g, and the sums / scales of its
-// accumulator columns 2t and 2t+1.
-struct XB8 {
-  uint2 b[8][3];
-  float2 sum[8];
-  float2 sx;  // column scales / 16
-};
-
-__device__ __forceinline__ void load_xb8(const uint8_t* rec, int g, int t, XB8& o) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-#pragma unroll
-    for (int s = 0; s < 3; ++s) o.b[j][s] = lds64(rec + ((j * 3 + s) * kXB + g) * 32 + 8 * t);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) o.sum[j] = *reinterpret_cast<const float2*>(rec + kXRecSum + (j * kXB + 2 * t) * 4);
-  const float2 sc = *reinterpret_cast<const float2*>(rec + kXRecScale + 2 * t * 4);
-  o.sx = make_float2(sc.x * (1.0f / 16.0f), sc.y * (1.0f / 16.0f));
-}
-
-// One 16-row Q4_K super-block tile against 8 columns: v[0], v[1] = rows g
-// and columns 2t, 2t+1; v[2], v[3] = row g + 8.
-__device__ __forceinline__ void tile8_q4k(const uint8_t* sm, uint32_t rg, uint32_t rg8, const XB8& xb, int t,
-                                          float (&v)[4]) {
+// One 16-row Q4_K super-block tile against 8 columns, the x operands read
+// from the prepared record `rec` in shared memory as they are used: v[0],
+// v[1] = row g and columns 2t, 2t+1; v[2], v[3] = row g + 8.
+__device__ __forceinline__ void tile8_q4k(const uint8_t* sm, uint32_t rg, uint32_t rg8, uint32_t rec, int g,
+                                          int t, float (&v)[4]) {
   const uint4 hg = lds128(sm, rg);
   const uint4 hg8 = lds128(sm, rg8);
   const uint32_t qo = rg + 16 + 8 * t, qo8 = rg8 + 16 + 8 * t;
   uint32_t scl, sch, ml, mh, scl8, sch8, ml8, mh8;
   MmaQ4K::sc_words(hg, scl, sch, ml, mh);
   MmaQ4K::sc_words(hg8, scl8, sch8, ml8, mh8);
+  const uint32_t xb = rec + g * 32 + 8 * t;  // B fragment of (j, slice s): xb + (j * 3 + s) * kXB * 32
   int alo[3][4], ahi[3][4];
 #pragma unroll
   for (int s = 0; s < 3; ++s)
@@ -970,11 +952,11 @@ __device__ __forceinline__ void tile8_q4k(const uint8_t* sm, uint32_t rg, uint32
     }
 #pragma unroll
     for (int s = 0; s < 3; ++s) {
+      const uint2 blo = lds64(sm, xb + ((2 * c) * 3 + s) * kXB * 32);
+      const uint2 bhi = lds64(sm, xb + ((2 * c + 1) * 3 + s) * kXB * 32);
       int dlo[4], dhi[4];
-      mma_k32_u8s8(q.x & 0x0F0F0F0Fu, q8.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, q8.y & 0x0F0F0F0Fu,
-                   xb.b[2 * c][s].x, xb.b[2 * c][s].y, dlo);
-      mma_k32_u8s8(q.x & 0xF0F0F0F0u, q8.x & 0xF0F0F0F0u, q.y & 0xF0F0F0F0u, q8.y & 0xF0F0F0F0u,
-                   xb.b[2 * c + 1][s].x, xb.b[2 * c + 1][s].y, dhi);
+      mma_k32_u8s8(q.x & 0x0F0F0F0Fu, q8.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, q8.y & 0x0F0F0F0Fu, blo.x, blo.y, dlo);
+      mma_k32_u8s8(q.x & 0xF0F0F0F0u, q8.x & 0xF0F0F0F0u, q.y & 0xF0F0F0F0u, q8.y & 0xF0F0F0F0u, bhi.x, bhi.y, dhi);
       alo[s][0] += sa * dlo[0];
       alo[s][1] += sa * dlo[1];
       alo[s][2] += sa8 * dlo[2];
@@ -995,36 +977,44 @@ __device__ __forceinline__ void tile8_q4k(const uint8_t* sm, uint32_t rg, uint32
     const int k = j & 3;
     const float m = static_cast<float>((mw >> (8 * k)) & 0xFFu);
     const float m8 = static_cast<float>((mw8 >> (8 * k)) & 0xFFu);
-    mg[0] = fmaf(m, xb.sum[j].x, mg[0]);
-    mg[1] = fmaf(m, xb.sum[j].y, mg[1]);
-    mg[2] = fmaf(m8, xb.sum[j].x, mg[2]);
-    mg[3] = fmaf(m8, xb.sum[j].y, mg[3]);
+    const float2 sj = *reinterpret_cast<const float2*>(sm + rec + kXRecSum + (j * kXB + 2 * t) * 4);
+    mg[0] = fmaf(m, sj.x, mg[0]);
+    mg[1] = fmaf(m, sj.y, mg[1]);
+    mg[2] = fmaf(m8, sj.x, mg[2]);
+    mg[3] = fmaf(m8, sj.y, mg[3]);
   }
+  const float2 sc = *reinterpret_cast<const float2*>(sm + rec + kXRecScale + 2 * t * 4);
+  const float sx0 = sc.x * (1.0f / 16.0f), sx1 = sc.y * (1.0f / 16.0f);
   float main[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     main[i] = static_cast<float>(16 * alo[0][i] + ahi[0][i]) +
               static_cast<float>(16 * alo[1][i] + ahi[1][i]) * (1.0f / 254.0f) +
               static_cast<float>(16 * alo[2][i] + ahi[2][i]) * (1.0f / 64516.0f);
-  v[0] = fmaf(d * xb.sx.x, main[0], -dmin * mg[0]);
-  v[1] = fmaf(d * xb.sx.y, main[1], -dmin * mg[1]);
-  v[2] = fmaf(d8 * xb.sx.x, main[2], -dmin8 * mg[2]);
-  v[3] = fmaf(d8 * xb.sx.y, main[3], -dmin8 * mg[3]);
+  v[0] = fmaf(d * sx0, main[0], -dmin * mg[0]);
+  v[1] = fmaf(d * sx1, main[1], -dmin * mg[1]);
+  v[2] = fmaf(d8 * sx0, main[2], -dmin8 * mg[2]);
+  v[3] = fmaf(d8 * sx1, main[3], -dmin8 * mg[3]);
 }
 
-__global__ void __launch_bounds__(288, 1) k_gemm8_q4k(const Gemm8Args a) {
+// Block = 1 producer warp + 8 consumer warps; a stage holds TPS = 8 / KC
+// row tiles of 16 rows x KC super-blocks, consumer warp w takes tile w / KC
+// and super-block w % KC.  Sized for two CTAs per SM.
+__global__ void __launch_bounds__(288, 2) k_gemm8_q4k(const Gemm8Args a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long row0 = static_cast<long long>(blockIdx.x) * a.rows_per_cta;
   long long row_end = row0 + a.rows_per_cta;
   if (row_end > a.rows) row_end = a.rows;
   if (row0 >= row_end) return;  // uniform across the CTA
+  const int TPS = 8 / a.KC, SR = 16 * TPS;
   const int nrows = static_cast<int>(row_end - row0);
-  const int ngroups = (nrows + 15) / 16;
+  const int ngroups = (nrows + SR - 1) / SR;
   const int nst = ngroups * a.NKC;  // stage s = (chunk s / ngroups, row group s % ngroups)
   const uint32_t XC = static_cast<uint32_t>(a.KC) * kXRec;
-  const uint32_t stage_bytes = 16u * static_cast<uint32_t>(a.GS);
-  float* red = reinterpret_cast<float*>(smem + a.off_red);  // [NS][16 rows][8 columns][8 warps]
+  const uint32_t stage_bytes = static_cast<uint32_t>(SR) * static_cast<uint32_t>(a.GS);
+  const int red_stage = SR * kXB * a.KC;  // floats: [KC warps][SR rows][8 columns]
+  float* red = reinterpret_cast<float*>(smem + a.off_red);
   float* acc = reinterpret_cast<float*>(smem + a.off_acc);  // [nrows][8]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
   uint64_t* empty = full + a.NS;
@@ -1062,14 +1052,14 @@ __global__ void __launch_bounds__(288, 1) k_gemm8_q4k(const Gemm8Args a) {
     };
     auto issue = [&](int s) {
       const int kc = s / ngroups, grp = s - kc * ngroups;
-      const int rows_g = min(16, nrows - 16 * grp);
+      const int rows_g = min(SR, nrows - SR * grp);
       const int seg = min(a.KC, a.NSB - kc * a.KC) * MmaQ4K::kSBBytes;
       const int b = s % a.NS;
       if (lane == 0) mbar_arrive_expect_tx(&full[b], static_cast<uint32_t>(rows_g * seg));
       __syncwarp();
-      if (lane < rows_g) {
-        const long long row = row0 + 16 * grp + lane;
-        bulk_g2s(smem + a.off_stage + b * stage_bytes + static_cast<size_t>(lane) * a.GS,
+      for (int r = lane; r < rows_g; r += 32) {
+        const long long row = row0 + SR * grp + r;
+        bulk_g2s(smem + a.off_stage + b * stage_bytes + static_cast<size_t>(r) * a.GS,
                  a.w + row * a.RB + static_cast<long long>(kc) * a.KC * MmaQ4K::kSBBytes, static_cast<uint32_t>(seg),
                  &full[b], policy);
       }
@@ -1084,22 +1074,6 @@ __global__ void __launch_bounds__(288, 1) k_gemm8_q4k(const Gemm8Args a) {
       ok = mbar_wait_bounded(&empty[buf], ph, kMmaTimeoutNs, abort_flag);
       if (!ok) break;
       const int kc = s / ngroups, grp = s - kc * ngroups;
-      const int rows_g = min(16, nrows - 16 * grp);
-      const float* rb = red + static_cast<size_t>(buf) * 16 * kXB * 8;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int idx = lane + 32 * q, r = idx >> 3, b = idx & 7;
-        if (r < rows_g) {
-          float v = 0.f;
-#pragma unroll
-          for (int w = 0; w < 8; ++w) v += rb[idx * 8 + w];
-          const int ar = (16 * grp + r) * kXB + b;
-          const float tot = acc[ar] + v;
-          acc[ar] = tot;
-          if (kc == a.NKC - 1 && b < a.cols) a.y[static_cast<long long>(b) * a.ldy + row0 + 16 * grp + r] = tot;
-        }
-      }
-      __syncwarp();
       if (s + a.NS < nst) {
         if (lane == 0) fence_proxy_async_smem();
         issue(s + a.NS);
@@ -1122,49 +1096,62 @@ __global__ void __launch_bounds__(288, 1) k_gemm8_q4k(const Gemm8Args a) {
   }
 
   // -------------------------------------------------- consumer warps
-  const int cw = warp - 1;  // super-block cw of every staged chunk
+  const int cw = warp - 1;
+  const int ti = cw / a.KC, sbw = cw % a.KC;  // row tile of the stage, super-block of the chunk
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t off_g = static_cast<uint32_t>(g * a.GS + cw * MmaQ4K::kSBBytes);
-  const uint32_t off_g8 = static_cast<uint32_t>((g + 8) * a.GS + cw * MmaQ4K::kSBBytes);
-  XB8 xb;
+  const uint32_t off_g = static_cast<uint32_t>((16 * ti + g) * a.GS + sbw * MmaQ4K::kSBBytes);
+  const uint32_t off_g8 = static_cast<uint32_t>((16 * ti + g + 8) * a.GS + sbw * MmaQ4K::kSBBytes);
   int buf = 0, loaded_kc = -1;
   uint32_t ph = 0;
   bool active = false;
   for (int s = 0; s < nst; ++s) {
-    const int kc = s / ngroups, grp = s - kc * ngroups;
+    const int kc = s / ngroups;
     if (kc != loaded_kc) {
       if (loaded_kc >= 0) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&xempty[loaded_kc & 1]);
       }
-      if (!mbar_wait_bounded(&xfull[kc & 1], (kc >> 1) & 1, kMmaTimeoutNs, abort_flag)) {
-        if (lane == 0) {
-          *abort_flag = 1;
-          atomicOr(a.status, kStatusCopyTimeout);
-        }
-        return;
-      }
-      active = cw < min(a.KC, a.NSB - kc * a.KC);
-      if (active) load_xb8(smem + (kc & 1) * XC + cw * kXRec, g, t, xb);
-      loaded_kc = kc;
-    }
-    if (!mbar_wait_bounded(&full[buf], ph, kMmaTimeoutNs, abort_flag)) {
-      if (lane == 0) {
+      // A wait that gives up flags the CTA and the loop runs on without the
+      // data, so every warp still reaches every named barrier below.
+      if (!mbar_wait_bounded(&xfull[kc & 1], (kc >> 1) & 1, kMmaTimeoutNs, abort_flag) && lane == 0) {
         *abort_flag = 1;
         atomicOr(a.status, kStatusCopyTimeout);
       }
-      return;
+      active = sbw < min(a.KC, a.NSB - kc * a.KC);
+      loaded_kc = kc;
     }
+    if (!mbar_wait_bounded(&full[buf], ph, kMmaTimeoutNs, abort_flag) && lane == 0) {
+      *abort_flag = 1;
+      atomicOr(a.status, kStatusCopyTimeout);
+    }
+    __syncwarp();
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t st = static_cast<uint32_t>(a.off_stage) + static_cast<uint32_t>(buf) * stage_bytes;
-    if (active) tile8_q4k(smem, st + off_g, st + off_g8, xb, t, v);
-    float* rb = red + static_cast<size_t>(buf) * 16 * kXB * 8;
-    rb[(g * kXB + 2 * t) * 8 + cw] = v[0];
-    rb[(g * kXB + 2 * t + 1) * 8 + cw] = v[1];
-    rb[((g + 8) * kXB + 2 * t) * 8 + cw] = v[2];
-    rb[((g + 8) * kXB + 2 * t + 1) * 8 + cw] = v[3];
+    if (active) tile8_q4k(smem, st + off_g, st + off_g8, (kc & 1) * XC + sbw * kXRec, g, t, v);
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[buf]);
+    if (lane == 0) mbar_arrive(&empty[buf]);  // the weights are consumed: the producer may refill
+    // partials [warp][row][column]: a warp's 32 lanes write 32 consecutive words per store
+    float* rb = red + static_cast<size_t>(buf) * red_stage;
+    const int r0 = 16 * ti + g, r8 = r0 + 8;
+    *reinterpret_cast<float2*>(rb + sbw * (SR * kXB) + r0 * kXB + 2 * t) = make_float2(v[0], v[1]);
+    *reinterpret_cast<float2*>(rb + sbw * (SR * kXB) + r8 * kXB + 2 * t) = make_float2(v[2], v[3]);
+    // The 8 consumer warps reduce the stage's partials together (fixed order,
+    // deterministic).  red[buf] is written again NS >= 2 stages later, after
+    // every warp has passed the next stage's barrier.
+    named_bar_sync(1, 256);
+    const int grp = s - kc * ngroups;
+    const int rows_g = min(SR, nrows - SR * grp);
+    for (int idx = cw * 32 + lane; idx < SR * kXB; idx += 256) {
+      const int r = idx >> 3, b = idx & 7;
+      if (r < rows_g) {
+        float sum = 0.f;
+        for (int w = 0; w < a.KC; ++w) sum += rb[w * (SR * kXB) + idx];
+        const int ar = (SR * grp + r) * kXB + b;
+        const float tot = acc[ar] + sum;
+        acc[ar] = tot;
+        if (kc == a.NKC - 1 && b < a.cols) a.y[static_cast<long long>(b) * a.ldy + row0 + SR * grp + r] = tot;
+      }
+    }
     if (++buf == a.NS) { buf = 0; ph ^= 1u; }
   }
 }
