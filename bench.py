@@ -612,6 +612,117 @@ def run_lmhead(args) -> int:
     return 0
 
 
+def run_decode(args) -> int:
+    """Decode only: the 1B-shaped greedy decode, `--steps` generated tokens
+    after a 128-token prompt and `--warmup` untimed steps, on 1 GPU or row-
+    sharded under torchrun.  value = tokens/s (device time, max over ranks)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from m3_avm_b200 import model
+    from m3_avm_b200.decoder import GpuDecoder
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    shape = model.LLAMA_1B
+    prompt = model.prompt_tokens(shape, DECODE_PROMPT, seed=2)
+    steps = max(1, min(args.steps, 2048))
+    max_pos = DECODE_PROMPT + args.warmup + steps + 8
+    if world > 1:
+        dec = GpuDecoder.from_torch_dist(shape, max_pos=max_pos, device=local, timeout_s=120)
+    else:
+        dec = GpuDecoder(shape, max_pos=max_pos, device=local)
+    dec.upload_all(model.synthetic_tensors(shape, seed=1))
+    dec.set_graph(not args.no_graph)
+    st = torch.cuda.ExternalStream(dec.stream, device=dev)
+    dec.prefill_logits(prompt)
+    dec.run_async(args.warmup)
+    dec.sync()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    dec.run_async(steps)
+    e1.record(st)
+    dec.sync()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    exchange = dec.exchange
+    dec.close()
+    peaks, kind = measured_peaks()
+    bytes_tok = shape.weight_bytes_per_token()
+    tok_s = steps / (ms / 1e3)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "1B decode tokens/sec", "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "llama-3.2-1b-shaped greedy decode, Q4_K_M mix", "prompt_tokens": DECODE_PROMPT,
+                       "parallelism": f"rows{world} ({exchange})" if world > 1 else "single GPU",
+                       "graph": not args.no_graph},
+            "roofline": {"bound": "hbm", "weight_bytes_per_token": bytes_tok,
+                         "achieved": round(bytes_tok * tok_s / 1e9, 1), "peak": float(peaks["hbm_gbs"]),
+                         "unit": "GB/s", "frac": round(bytes_tok * tok_s / 1e9 / float(peaks["hbm_gbs"]), 4),
+                         "peak_kind": kind},
+            "gpu_launches": steps * (1 + 5 * shape.n_layers + 2),
+            "clocks": clocks,
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_batched(args) -> int:
+    """One batched Q4_K 28672 x 8192 GEMM with X of --batch columns, `--steps`
+    timed launches over rotating weight copies (a small case for profiling)."""
+    import torch
+
+    from m3_avm_b200 import synth
+    from m3_avm_b200.inference_gpu import GpuOffload
+
+    dev = torch.device("cuda", 0)
+    B = args.batch
+    raw = synth.weights(DTYPE, BATCHED_IN, BATCHED_OUT, seed=5)
+    n_copies = 2
+    g = GpuOffload.try_new(BATCHED_IN, BATCHED_OUT, device=0)
+    for c in range(n_copies):
+        g.upload(c, DTYPE, raw, BATCHED_IN, BATCHED_OUT)
+    X = torch.from_numpy(synth.activations(BATCHED_IN, seed=6, batch=B)).to(dev)
+    Y = torch.empty((B, BATCHED_OUT), dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        g.matvec_dev(i % n_copies, X, Y, stream=st.cuda_stream)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(args.steps):
+        g.matvec_dev(i % n_copies, X, Y, stream=st.cuda_stream)
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    g.close()
+    abytes = algorithmic_bytes(BATCHED_IN, BATCHED_OUT, DTYPE, batch=B)
+    print(json.dumps({"metric": f"Q4_K batched GEMM effective GB/s @{BATCHED_OUT}x{BATCHED_IN}, B={B}",
+                      "value": round(abytes / us / 1e3, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5), "higher_is_better": True,
+                      "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                      "config": {"workload": f"q4k_batched_{BATCHED_OUT}x{BATCHED_IN}", "batch": B,
+                                 "weight_copies": n_copies},
+                      "tflops": round(2.0 * B * BATCHED_IN * BATCHED_OUT / us / 1e6, 2)}), flush=True)
+    return 0
+
+
 def ctypes_status(lib, device):
     import ctypes
 
@@ -632,15 +743,21 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the 1B decode tokens/s leg")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched Q4_K 28672x8192 sweep")
-    ap.add_argument("--workload", choices=["gemv", "lmhead"], default="gemv",
-                    help="gemv: Q4_K 14336x4096 GEMV per GPU (the headline); "
-                         "lmhead: Q6_K 128256x4096 rows sharded over the GPUs + all-gather")
+    ap.add_argument("--workload", choices=["gemv", "lmhead", "decode", "batched"], default="gemv",
+                    help="gemv: Q4_K 14336x4096 GEMV per GPU (the headline, with the decode and batched legs); "
+                         "lmhead: Q6_K 128256x4096 rows sharded over the GPUs + all-gather; "
+                         "decode: the 1B decode alone (--steps tokens); batched: one Q4_K 28672x8192 GEMM")
+    ap.add_argument("--batch", type=int, default=8, help="columns of X for --workload batched")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "lmhead":
         return run_lmhead(args)
+    if args.workload == "decode":
+        return run_decode(args)
+    if args.workload == "batched":
+        return run_batched(args)
     return run_ours(args)
 
 

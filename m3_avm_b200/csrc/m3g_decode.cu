@@ -8,9 +8,9 @@
 //   per layer:
 //     GEMV  qkv       rms_norm(hidden) * attn_norm, fused into the GEMV input;
 //                     q|k|v rows concatenated into one weight when they share a dtype
-//     k_attention     RoPE of q and k, K/V appended at pos, softmax attention
-//                     over positions [0, pos] per query head (GQA: head hh reads
-//                     KV head hh / (n_heads / n_kv_heads))
+//     k_attention_split  RoPE of q and k, K/V appended at pos, softmax attention
+//                     over positions [0, pos], one 8-CTA cluster per query head
+//                     (GQA: head hh reads KV head hh / (n_heads / n_kv_heads))
 //     GEMV  o         hidden += W_o att (residual fused in the epilogue)
 //     GEMV  gate|up   rms_norm(hidden) * ffn_norm input, gate and up rows
 //                     interleaved in blocks of 8 so the epilogue writes silu(g) * u
@@ -40,6 +40,7 @@
 #include <cstring>
 #include <vector>
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <nccl.h>
@@ -57,11 +58,10 @@ int nccl_comm_create(int rank, int world, const uint8_t* id128, double timeout_s
 void nccl_comm_close(ncclComm_t comm, double timeout_s);
 }  // namespace m3g
 
+namespace cg = cooperative_groups;
+
 namespace m3g {
 namespace {
-
-constexpr int kAttnThreads = 256;
-constexpr int kAttnWarps = kAttnThreads / 32;
 
 struct AttnArgs {
   const float* qkv;   // [q: n_heads*HD][k: kvd][v: kvd]
@@ -78,54 +78,66 @@ struct AttnArgs {
   float scale;        // 1 / sqrt(HD)
 };
 
-// One CTA per query head.  Scores use the reference's sequential dot product
-// (products and sums each rounded, in index order), so they are bit-identical
-// to it for identical q and k; the softmax sum and the weighted V sum are
-// reduced in a different order.
+// Attention of one step, one thread-block cluster of kAttnSplit CTAs per
+// query head: RoPE of q and of the head's KV-group k (split-half pairs,
+// rounded as the reference's apply_rope), the first CTA of the group's first
+// head appends K/V at pos, and each CTA takes a contiguous slice of the
+// positions with a local softmax (max m, sum l, weighted V o).  Scores are
+// the reference's sequential dot products (bit-identical for identical q and
+// k).  CTA 0 of the cluster reads the others' partials through distributed
+// shared memory and combines them, out = sum_p e^(m_p - M) o_p / sum_p
+// e^(m_p - M) l_p (GQA: query head hh reads KV head hh / groups).
+constexpr int kAttnSplit = 8;
+constexpr int kAttnSplitThreads = 128;
+
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
-  constexpr int HALF = HD / 2, DPL = HD / 32;
+__global__ void __launch_bounds__(kAttnSplitThreads) k_attention_split(const AttnArgs a) {
+  constexpr int HALF = HD / 2, DPL = HD / 32, NW = kAttnSplitThreads / 32;
   extern __shared__ __align__(16) float sm[];
-  float* qs = sm;                  // [HD] rotated q
-  float* kn = qs + HD;             // [HD] rotated k of this position
-  float* vn = kn + HD;             // [HD] v of this position
-  float* part = vn + HD;           // [warps][HD] partial outputs
-  float* red = part + kAttnWarps * HD;  // [64] reductions
-  float* sc = red + 64;            // [max_pos] scores, then weights
+  float* qs = sm;                  // [HD]
+  float* kn = qs + HD;             // [HD]
+  float* vn = kn + HD;             // [HD]
+  float* part = vn + HD;           // [NW][HD]
+  float* red = part + NW * HD;     // [64]
+  float* res = red + 64;           // [2 + HD]: m, l, o of this CTA (read by CTA 0)
+  float* sc = res + 2 + HD;        // [chunk] scores, then weights
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hh = blockIdx.x, kv = hh / a.groups;
+  const int hh = blockIdx.x / kAttnSplit, kv = hh / a.groups;
   grid_dep_wait();
   grid_dep_launch();
   const int pos = *a.pos;
-  if (pos < 0 || pos >= a.max_pos) {
-    if (tid == 0) atomicOr(a.status, kStatusBadPos);
-    return;
-  }
-  const float* cs = a.rope + static_cast<size_t>(pos) * HD;
-  if (tid < HALF) {
-    const float c = cs[2 * tid], s = cs[2 * tid + 1];
+  const bool pos_ok = pos >= 0 && pos < a.max_pos;
+  if (!pos_ok && tid == 0 && rank == 0 && hh == 0) atomicOr(a.status, kStatusBadPos);
+  const int npos = pos_ok ? pos + 1 : 0;
+  const int chunk = (npos + kAttnSplit - 1) / kAttnSplit;
+  const int i0 = min(npos, rank * chunk), i1 = min(npos, i0 + chunk);
+  if (pos_ok) {
+    const float* cs = a.rope + static_cast<size_t>(pos) * HD;
     const float* q = a.qkv + hh * HD;
     const float* k = a.qkv + a.qd + kv * HD;
-    float x0 = q[tid], x1 = q[tid + HALF];
-    qs[tid] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    qs[tid + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-    x0 = k[tid];
-    x1 = k[tid + HALF];
-    kn[tid] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    kn[tid + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-  } else if (tid < HALF + HD) {
-    vn[tid - HALF] = a.qkv[a.qd + a.kvd + kv * HD + tid - HALF];
+    for (int i = tid; i < HALF; i += kAttnSplitThreads) {
+      const float c = cs[2 * i], s = cs[2 * i + 1];
+      float x0 = q[i], x1 = q[i + HALF];
+      qs[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+      qs[i + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+      x0 = k[i];
+      x1 = k[i + HALF];
+      kn[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+      kn[i + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    }
+    for (int i = tid; i < HD; i += kAttnSplitThreads) vn[i] = a.qkv[a.qd + a.kvd + kv * HD + i];
   }
   __syncthreads();
-  // The first query head of each KV group appends this position's K and V;
-  // every head reads position pos from shared memory, so no CTA waits for it.
-  if (hh % a.groups == 0 && tid < HD) {
-    a.kc[static_cast<size_t>(pos) * a.kvd + kv * HD + tid] = kn[tid];
-    a.vc[static_cast<size_t>(pos) * a.kvd + kv * HD + tid] = vn[tid];
+  if (pos_ok && rank == 0 && hh % a.groups == 0) {
+    for (int i = tid; i < HD; i += kAttnSplitThreads) {
+      a.kc[static_cast<size_t>(pos) * a.kvd + kv * HD + i] = kn[i];
+      a.vc[static_cast<size_t>(pos) * a.kvd + kv * HD + i] = vn[i];
+    }
   }
-  const int npos = pos + 1;
   float lmax = -INFINITY;
-  for (int i = tid; i < npos; i += kAttnThreads) {
+  for (int i = i0 + tid; i < i1; i += kAttnSplitThreads) {
     const float* kr = i == pos ? kn : a.kc + static_cast<size_t>(i) * a.kvd + kv * HD;
     float dot = 0.f;
 #pragma unroll
@@ -138,7 +150,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
       dot = __fadd_rn(dot, __fmul_rn(q4.w, k4.w));
     }
     const float s = __fmul_rn(dot, a.scale);
-    sc[i] = s;
+    sc[i - i0] = s;
     lmax = fmaxf(lmax, s);
   }
 #pragma unroll
@@ -147,27 +159,22 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   __syncthreads();
   float mx = red[0];
 #pragma unroll
-  for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, red[w]);
+  for (int w = 1; w < NW; ++w) mx = fmaxf(mx, red[w]);
   float lsum = 0.f;
-  for (int i = tid; i < npos; i += kAttnThreads) {
-    const float e = expf(__fsub_rn(sc[i], mx));
-    sc[i] = e;
+  for (int i = i0 + tid; i < i1; i += kAttnSplitThreads) {
+    const float e = expf(__fsub_rn(sc[i - i0], mx));
+    sc[i - i0] = e;
     lsum += e;
   }
   lsum = warp_sum(lsum);
   if (lane == 0) red[32 + warp] = lsum;
   __syncthreads();
-  float sum = 0.f;
-#pragma unroll
-  for (int w = 0; w < kAttnWarps; ++w) sum += red[32 + w];
-  for (int i = tid; i < npos; i += kAttnThreads) sc[i] = __fdiv_rn(sc[i], sum);
-  __syncthreads();
   float acc[DPL];
 #pragma unroll
   for (int d = 0; d < DPL; ++d) acc[d] = 0.f;
 #pragma unroll 4
-  for (int i = warp; i < npos; i += kAttnWarps) {
-    const float w = sc[i];
+  for (int i = i0 + warp; i < i1; i += NW) {
+    const float w = sc[i - i0];
     const float* vr = (i == pos ? vn : a.vc + static_cast<size_t>(i) * a.kvd + kv * HD) + DPL * lane;
     if (DPL == 2) {
       const float2 v2 = *reinterpret_cast<const float2*>(vr);
@@ -187,12 +194,37 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
 #pragma unroll
   for (int d = 0; d < DPL; ++d) part[warp * HD + DPL * lane + d] = acc[d];
   __syncthreads();
-  if (tid < HD) {
+  for (int i = tid; i < HD; i += kAttnSplitThreads) {
     float o = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) o += part[w * HD + tid];
-    a.out[hh * HD + tid] = o;
+    for (int w = 0; w < NW; ++w) o += part[w * HD + i];
+    res[2 + i] = o;
   }
+  if (tid == 0) {
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) l += red[32 + w];
+    res[0] = i1 > i0 ? mx : -INFINITY;
+    res[1] = l;
+  }
+  cluster.sync();  // every CTA's partial is in its shared memory
+  if (rank == 0) {
+    for (int i = tid; i < HD; i += kAttnSplitThreads) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int p = 0; p < kAttnSplit; ++p) M = fmaxf(M, cluster.map_shared_rank(res, p)[0]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int p = 0; p < kAttnSplit; ++p) {
+        const float* r = cluster.map_shared_rank(res, p);
+        const float f = r[0] == -INFINITY ? 0.f : expf(__fsub_rn(r[0], M));
+        L = fmaf(f, r[1], L);
+        O = fmaf(f, r[2 + i], O);
+      }
+      if (pos_ok) a.out[hh * HD + i] = __fdiv_rn(O, L);
+    }
+  }
+  cluster.sync();  // the partials stay readable until CTA 0 has combined them
 }
 
 // hidden = row tokens[pos] of the embedding, decoded exactly as the
@@ -264,6 +296,26 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+template <class Kern, class... Args>
+cudaError_t launch_pdl_cluster(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster,
+                               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
@@ -344,6 +396,14 @@ struct m3g_decoder {
 };
 
 namespace {
+
+// Shared memory of k_attention_split: q, k, v of this position, per-warp
+// partials, reductions, the CTA's (m, l, o) and its slice of the scores.
+size_t attn_split_smem(const m3g_decoder* d) {
+  const size_t hd = static_cast<size_t>(d->hd), nw = m3g::kAttnSplitThreads / 32;
+  const size_t chunk = (d->cfg.max_pos + m3g::kAttnSplit - 1) / m3g::kAttnSplit;
+  return sizeof(float) * (3 * hd + nw * hd + 64 + 2 + hd + chunk);
+}
 
 // Rank p's copy of a region offset (this rank's own region for p == rank).
 template <class T>
@@ -502,7 +562,7 @@ int enqueue_step(m3g_decoder* d) {
   DEC_CUDA(m3g::launch_pdl(m3g::k_embed, dim3((h + 255) / 256), dim3(256), 0, d->st, static_cast<const uint8_t*>(E.d),
                            static_cast<int>(E.dtype), be, bb, static_cast<const int*>(d->tokens),
                            static_cast<const int*>(d->dpos), d->hidden, h, V, mp, d->status));
-  const size_t attn_smem = sizeof(float) * (3 * d->hd + m3g::kAttnWarps * d->hd + 64 + static_cast<size_t>(mp));
+  const size_t split_smem = attn_split_smem(d);
   for (int l = 0; l < L; ++l) {
     const Tensor* T = &d->t[kSlotLayer0 + kPerLayer * l];
     const float* g_attn = reinterpret_cast<const float*>(T[kAttnNorm].d);
@@ -538,11 +598,14 @@ int enqueue_step(m3g_decoder* d) {
     a.qd = h;
     a.max_pos = mp;
     a.scale = 1.0f / sqrtf(static_cast<float>(d->hd));
-    const dim3 agrid(static_cast<unsigned>(d->cfg.n_heads));
+    const dim3 sgrid(static_cast<unsigned>(d->cfg.n_heads * m3g::kAttnSplit));
+    const dim3 sblock(m3g::kAttnSplitThreads);
     if (d->hd == 64) {
-      DEC_CUDA(m3g::launch_pdl(m3g::k_attention<64>, agrid, dim3(m3g::kAttnThreads), attn_smem, d->st, a));
+      DEC_CUDA(m3g::launch_pdl_cluster(m3g::k_attention_split<64>, sgrid, sblock, split_smem, d->st, m3g::kAttnSplit,
+                                       a));
     } else {
-      DEC_CUDA(m3g::launch_pdl(m3g::k_attention<128>, agrid, dim3(m3g::kAttnThreads), attn_smem, d->st, a));
+      DEC_CUDA(m3g::launch_pdl_cluster(m3g::k_attention_split<128>, sgrid, sblock, split_smem, d->st,
+                                       m3g::kAttnSplit, a));
     }
     if (int rc = gemv(d, part(T[kO]), d->att, nullptr, nullptr, d->hidden, m3g::kXPlain, d->hidden)) return rc;
     if (pp) {  // this rank's rows, stored into every rank's buffers by the GEMV epilogues
@@ -853,11 +916,11 @@ M3G_API int m3g_decoder_create_sharded(int device, const m3g_decoder_config* cfg
   if (e == cudaSuccess) e = cudaMemset(d->dpos, 0, 4 * 4);
   if (e == cudaSuccess) e = cudaMemset(d->tokens, 0, 4 * (mp + 1));
   if (e == cudaSuccess) {
-    const size_t attn_smem = sizeof(float) * (3 * hd + m3g::kAttnWarps * hd + 64 + mp);
-    e = hd == 64 ? cudaFuncSetAttribute(m3g::k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(attn_smem))
-                 : cudaFuncSetAttribute(m3g::k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(attn_smem));
+    const int split_smem = static_cast<int>(attn_split_smem(d));
+    e = hd == 64 ? cudaFuncSetAttribute(m3g::k_attention_split<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        split_smem)
+                 : cudaFuncSetAttribute(m3g::k_attention_split<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        split_smem);
   }
   if (e != cudaSuccess) return fail(host_fail(M3G_ECUDA, "decoder setup: %s", cudaGetErrorString(e)));
   if (world > 1) {
