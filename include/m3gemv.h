@@ -285,6 +285,28 @@ M3G_API void* m3g_decoder_stream(const m3g_decoder* dec);
 M3G_API int m3g_decoder_set_graph(m3g_decoder* dec, int use_graph);
 M3G_API void m3g_decoder_destroy(m3g_decoder* dec);
 
+/* ---------------------------------------------------------------- VM opcodes MATVEC and FFN
+ *
+ * The MATVEC opcode (exec_matvec, src/vm.rs:2643-2685): y[M][N] from x[M][K]
+ * (f32) and W of K*N elements (F32, F16 or a block dtype).  M = 1 keeps the
+ * reference's matvec::matvec orientation y[j] = sum_i x[i] W[i + j*K] (the
+ * fused GEMV for block dtypes); M > 1 keeps its ndarray reading of W as a
+ * row-major [K, N] array, y[m][j] = sum_k x[m][k] W[k*N + j].  Device
+ * pointers, enqueued on `stream`.  Differences: W is decoded by its ggml
+ * dtype (read_f32_tensor, src/memory.rs:1331-1338, decodes a memory::DType
+ * Q8_0 tensor with the Q4_K decoder); the row-major sums use another order. */
+M3G_API int m3g_vm_matvec_dev(const float* x, uint64_t M, uint64_t K, const uint8_t* w, uint64_t w_len,
+                              uint32_t dtype, uint64_t N, float* y, void* stream);
+/* The FFN opcode (exec_ffn, src/vm.rs:2471-2576): hidden = x W1 + b1,
+ * gated = hidden * sigmoid(hidden), y = gated W2 + b2, x [M][D], W1 row-major
+ * [D, H], W2 row-major [H, D_out]; a bias of length H (D_out) is broadcast
+ * over the rows, of length M*H (M*D_out) taken per row, any other length (or
+ * NULL) is zero.  The hidden buffer is stream-ordered (cudaMallocAsync). */
+M3G_API int m3g_vm_ffn_dev(const float* x, uint64_t M, uint64_t D, const uint8_t* w1, uint64_t w1_len,
+                           uint32_t dtype1, uint64_t H, const uint8_t* w2, uint64_t w2_len, uint32_t dtype2,
+                           uint64_t D_out, const float* b1, uint64_t b1_len, const float* b2, uint64_t b2_len,
+                           float* y, void* stream);
+
 /* ---------------------------------------------------------------- greedy head without allocation
  *
  * No counterpart in the reference.  *token (device memory) = the greedy pick

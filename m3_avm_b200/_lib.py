@@ -91,6 +91,9 @@ SIGNATURES: dict[str, tuple] = {
     "m3g_decoder_set_graph": (ctypes.c_int, [_vp, ctypes.c_int]),
     "m3g_decoder_destroy": (None, [_vp]),
     "m3g_matvec_greedy_noalloc": (ctypes.c_int, [_vp, _vp, _u64, _u32, _u64, _u64, _vp, _vp]),
+    "m3g_vm_matvec_dev": (ctypes.c_int, [_vp, _u64, _u64, _vp, _u64, _u32, _u64, _vp, _vp]),
+    "m3g_vm_ffn_dev": (ctypes.c_int, [_vp, _u64, _u64, _vp, _u64, _u32, _u64, _vp, _u64, _u32, _u64, _vp, _u64,
+                                      _vp, _u64, _vp, _vp]),
 }
 
 _lib = None
