@@ -93,6 +93,8 @@ struct Tuning {
   int64_t decode_xfirst = 0;      // the same for the GEMVs of a decode step
   int64_t decode_p2p = 1;         // sharded decode: peer stores over NVLink instead of NCCL all-gathers
   int64_t gemm8 = 1;              // batched Q4_K: 8 columns per launch (k_gemm8_q4k) instead of one GEMV each
+  int64_t umma = 1;               // batched Q4_K on tcgen05 (k_umma_q4k), up to 64 columns per pass
+  int64_t umma_chains = 8;        // independent accumulators per super-block (capped by TMEM)
 };
 Tuning g_tune;
 
@@ -371,8 +373,85 @@ bool plan_gemm8(const FmtInfo& f, long long in_dim, long long rows, const uint8_
   return static_cast<long long>(p.smem) <= budget;
 }
 
+// Batched Q4_K on tcgen05: NB accumulator columns for a pass of `cols`
+// columns; weight stages of one 128-row super-block tile, X stages of one
+// prepared super-block, as many of each as shared memory holds (the request is
+// above half an SM, so one CTA -- and one 512-column TMEM allocation -- per SM).
+struct UmmaPlan {
+  m3g::UmmaArgs a{};
+  int grid = 0, nb = 0;
+  size_t smem = 0;
+  size_t off_cnt = 0, off_xt = 0, off_part = 0, ws_bytes = 0;
+};
+
+bool plan_umma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t* w, long long cols,
+               const DevState& ds, UmmaPlan& p) {
+  if (f.fmt != 12 || in_dim % 256 || in_dim > (1 << 22) || cols < 1 || cols > 64) return false;
+  if (reinterpret_cast<uintptr_t>(w) % 16 || rows < 1 || rows > (1ll << 31) - 1) return false;
+  const int nb = cols <= 16 ? 16 : cols <= 32 ? 32 : 64;
+  const long long XS = m3g::umma_xtile(nb), SW = 128 * 144;
+  const long long avail = std::min<long long>(ds.smem_optin, 232448) - 8192 - 4096 - 256;
+  long long NSX = 0, NSW = 0;
+  for (long long nx = 4; nx >= 2 && !NSX; --nx) {
+    const long long nw = std::min<long long>(8, (avail - nx * XS) / SW);
+    if (nw >= 4 || (nx == 2 && nw >= 2)) NSX = nx, NSW = nw;
+  }
+  if (!NSX) return false;
+  const long long NSB = in_dim / 256, tiles = (rows + 127) / 128;
+  p.nb = nb;
+  p.a.RB = NSB * 144;
+  p.a.rows = rows;
+  p.a.NSB = static_cast<int>(NSB);
+  p.a.tiles = static_cast<int>(tiles);
+  p.a.T = tiles * NSB;
+  p.a.NSW = static_cast<int>(NSW);
+  p.a.NSX = static_cast<int>(NSX);
+  p.a.off_x = static_cast<int>(NSW * SW);
+  p.a.off_am = static_cast<int>(p.a.off_x + NSX * XS);
+  p.a.off_bar = p.a.off_am + 8192 + 4096;  // m operand stages, (d, dmin) ring
+  p.smem = static_cast<size_t>(p.a.off_bar + (2 * NSW + NSX + 12) * 8 + 16);
+  p.grid = static_cast<int>(std::min<long long>(ds.sms, p.a.T));
+  p.off_cnt = 256;  // 64 column exponents first
+  p.off_xt = p.off_cnt + static_cast<size_t>((tiles * 4 + 255) / 256 * 256);
+  p.off_part = p.off_xt + static_cast<size_t>(NSB * XS);
+  p.ws_bytes = p.off_part + static_cast<size_t>(p.grid) * 2 * nb * 128 * sizeof(float);
+  return static_cast<long long>(p.smem) <= std::min<long long>(ds.smem_optin, 232448) &&
+         static_cast<long long>(p.smem) > ds.smem_per_sm / 2;
+}
+
 int gemv_batch_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const float* x, float* y,
                       long long in_dim, long long out_dim, long long batch, cudaStream_t st) {
+  UmmaPlan up;
+  if (batch >= 2 && !g_tune.force_generic && g_tune.mma && g_tune.umma &&
+      plan_umma(f, in_dim, out_dim, w, std::min<long long>(batch, 64), ds, up)) {
+    // one workspace sized for the widest pass: exponents | tile counters | X tiles | partial tiles
+    uint8_t* ws = nullptr;
+    M3G_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), up.ws_bytes, st));
+    int rc = M3G_OK;
+    for (long long p0 = 0; p0 < batch && rc == M3G_OK; p0 += 64) {
+      const long long cols = std::min<long long>(64, batch - p0);
+      UmmaPlan pp;
+      if (!plan_umma(f, in_dim, out_dim, w, cols, ds, pp)) {
+        rc = fail(M3G_EINVAL, "no tcgen05 plan for %lld columns", cols);
+        break;
+      }
+      pp.a.w = w;
+      pp.a.xexp = reinterpret_cast<const int*>(ws);
+      pp.a.cnt = reinterpret_cast<unsigned*>(ws + pp.off_cnt);
+      pp.a.xt = ws + pp.off_xt;
+      pp.a.part = reinterpret_cast<float*>(ws + pp.off_part);
+      pp.a.y = y + p0 * out_dim;
+      pp.a.status = ds.status;
+      pp.a.cols = static_cast<int>(cols);
+      pp.a.ldy = static_cast<int>(out_dim);
+      cudaError_t e = m3g::launch_umma_q4k(pp.a, x + p0 * in_dim, in_dim, pp.nb,
+                                           static_cast<int>(g_tune.umma_chains), pp.grid, pp.smem, st);
+      if (e != cudaSuccess) rc = cuda_fail(e, "tcgen05 batched GEMV launch");
+      else g_launches.fetch_add(3, std::memory_order_relaxed);
+    }
+    cudaFreeAsync(ws, st);
+    return rc;
+  }
   Gemm8Plan gp;
   if (batch >= 2 && !g_tune.force_generic && g_tune.mma && g_tune.gemm8 && plan_gemm8(f, in_dim, out_dim, w, x, ds, gp)) {
     // X is quantised once per pass of 8 columns into a stream-ordered workspace.
@@ -602,6 +681,8 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "decode_xfirst")) g_tune.decode_xfirst = value != 0;
   else if (!strcmp(key, "decode_p2p")) g_tune.decode_p2p = value != 0;
   else if (!strcmp(key, "gemm8")) g_tune.gemm8 = value != 0;
+  else if (!strcmp(key, "umma")) g_tune.umma = value != 0;
+  else if (!strcmp(key, "umma_chains") && value >= 1 && value <= 8) g_tune.umma_chains = value;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }

@@ -149,6 +149,24 @@ struct Gemm8Args {
 cudaError_t launch_xprep8(const float* x, int cols, int in_dim, uint8_t* out, cudaStream_t st);
 cudaError_t launch_gemm8_q4k(const Gemm8Args& a, int grid, size_t smem, cudaStream_t st);
 
+// Batched Q4_K on tcgen05 (m3g_umma.cu): up to 64 columns per pass, NB = 16,
+// 32 or 64 accumulator columns, 128-row tiles split evenly over the CTAs.
+struct UmmaArgs {
+  const uint8_t* w;   // Q4_K rows, RB bytes apart
+  const uint8_t* xt;  // prepared X tiles, umma_xtile(NB) bytes per super-block
+  const int* xexp;    // per-column power-of-two exponents of X
+  unsigned* cnt;      // per-tile super-block counters (zeroed by the X prep)
+  float* part;        // [grid][2][NB][128] partial tiles
+  float* y;           // y[col * ldy + row]
+  uint32_t* status;
+  long long RB, rows, T;  // T = tiles * NSB iterations
+  int NSB, cols, ldy, tiles, NSW, NSX;
+  int off_x, off_am, off_bar;
+};
+cudaError_t launch_umma_q4k(const UmmaArgs& a, const float* x, long long in_dim, int nb, int chains, int grid,
+                            size_t smem, cudaStream_t st);
+int umma_xtile(int nb);
+
 int mma_sb_bytes(int fmt);
 cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
                             bool pdl);

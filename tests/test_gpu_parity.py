@@ -334,8 +334,12 @@ def test_gemm8_batched_q4k_matches_oracle(m3, in_dim, out_dim, batch):
     dev = torch.device("cuda:0")
     xd = torch.from_numpy(X).to(dev)
     rd = torch.from_numpy(raw).to(dev)
-    Y = m3.matvec_quant.matvec_quant_dev(xd, rd, 12, in_dim, out_dim)
-    torch.cuda.synchronize()
+    m3.matvec_quant.set_tuning("umma", 0)  # the 8-column mma.sync kernel
+    try:
+        Y = m3.matvec_quant.matvec_quant_dev(xd, rd, 12, in_dim, out_dim)
+        torch.cuda.synchronize()
+    finally:
+        m3.matvec_quant.set_tuning("umma", 1)
     Yh = Y.cpu().numpy()
     for b in range(batch):
         check_gemv(Yh[b], raw, 12, in_dim, out_dim, X[b])
@@ -351,12 +355,14 @@ def test_gemm8_equals_per_column_gemv(m3):
     X = m3.synth.activations(in_dim, seed=4, batch=batch)
     dev = torch.device("cuda:0")
     xd, rd = torch.from_numpy(X).to(dev), torch.from_numpy(raw).to(dev)
-    a = m3.matvec_quant.matvec_quant_dev(xd, rd, 12, in_dim, out_dim)
-    m3.matvec_quant.set_tuning("gemm8", 0)
+    m3.matvec_quant.set_tuning("umma", 0)  # the 8-column mma.sync kernel
     try:
+        a = m3.matvec_quant.matvec_quant_dev(xd, rd, 12, in_dim, out_dim)
+        m3.matvec_quant.set_tuning("gemm8", 0)
         b = m3.matvec_quant.matvec_quant_dev(xd, rd, 12, in_dim, out_dim)
     finally:
         m3.matvec_quant.set_tuning("gemm8", 1)
+        m3.matvec_quant.set_tuning("umma", 1)
     torch.cuda.synchronize()
     for k in range(batch):
         bound = gemv_bound(raw, 12, in_dim, out_dim, X[k])
