@@ -243,8 +243,12 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   // Whole rows are contiguous when one k-chunk covers the row: copy 4 rows
   // per bulk copy then; otherwise one copy per row segment.
   const long long CG = (NKC == 1 && g_tune.mma_cg == 4) ? 4 : 1;
+  // Row-group stride: the residue mod 128 that makes the tile's shared loads
+  // conflict-free (Q4_K: 16-byte header + 8-byte quant loads of 8 rows; the
+  // 2-byte aligned blocks of Q6_K and Q4_0: 4-byte loads across two words).
+  const long long gs_mod = f.fmt == 12 ? 32 : 16;
   long long GS = (CG * seg + 15) / 16 * 16;
-  while (GS % 128 != 32) GS += 16;
+  while (GS % 128 != gs_mod) GS += 16;
   const long long xsl = 3 * in_dim, s32 = in_dim / 8, s16 = in_dim / 4, sc = NSB * 4;
   const long long fixed = xsl + s32 + s16 + sc + 4 * 128 + 16;
   const long long mctas = std::max<int64_t>(1, g_tune.mma_ctas);

@@ -55,7 +55,7 @@ struct MmaArgs {
   int KC;             // super-blocks per k-chunk
   int NKC;            // k-chunks per tile
   int CG;             // rows per bulk copy: 4 (whole rows, NKC == 1) or 1 (row segments)
-  int GS;             // shared-memory stride between copy groups (32 mod 128 bytes)
+  int GS;             // shared-memory stride between copy groups (32 mod 128 bytes for Q4_K, 16 otherwise)
   int SEG;            // bytes of one row's segment within a group
   int NS;             // stages
   int PRE;            // stages issued before the grid dependency resolves
