@@ -415,7 +415,7 @@ bool plan_umma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t
   p.a.off_bar = p.a.off_am + 8192 + 4096;  // m operand stages, (d, dmin) ring
   p.smem = static_cast<size_t>(p.a.off_bar + (2 * NSW + NSX + 12) * 8 + 16);
   p.grid = static_cast<int>(std::min<long long>(ds.sms, p.a.T));
-  p.off_cnt = 256;  // 64 column exponents first
+  p.off_cnt = static_cast<size_t>((NSB * 64 * 4 + 255) / 256 * 256);  // column scales [NSB][<= 64] first
   p.off_xt = p.off_cnt + static_cast<size_t>((tiles * 4 + 255) / 256 * 256);
   p.off_part = p.off_xt + static_cast<size_t>(NSB * XS);
   p.ws_bytes = p.off_part + static_cast<size_t>(p.grid) * 2 * nb * 128 * sizeof(float);
@@ -428,7 +428,7 @@ int gemv_batch_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, co
   UmmaPlan up;
   if (batch >= 2 && !g_tune.force_generic && g_tune.mma && g_tune.umma &&
       plan_umma(f, in_dim, out_dim, w, std::min<long long>(batch, 64), ds, up)) {
-    // one workspace sized for the widest pass: exponents | tile counters | X tiles | partial tiles
+    // one workspace sized for the widest pass: column scales | tile counters | X tiles | partial tiles
     uint8_t* ws = nullptr;
     M3G_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), up.ws_bytes, st));
     int rc = M3G_OK;
@@ -440,7 +440,7 @@ int gemv_batch_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, co
         break;
       }
       pp.a.w = w;
-      pp.a.xexp = reinterpret_cast<const int*>(ws);
+      pp.a.sig = reinterpret_cast<const float*>(ws);
       pp.a.cnt = reinterpret_cast<unsigned*>(ws + pp.off_cnt);
       pp.a.xt = ws + pp.off_xt;
       pp.a.part = reinterpret_cast<float*>(ws + pp.off_part);

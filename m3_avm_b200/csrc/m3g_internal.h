@@ -154,7 +154,7 @@ cudaError_t launch_gemm8_q4k(const Gemm8Args& a, int grid, size_t smem, cudaStre
 struct UmmaArgs {
   const uint8_t* w;   // Q4_K rows, RB bytes apart
   const uint8_t* xt;  // prepared X tiles, umma_xtile(NB) bytes per super-block
-  const int* xexp;    // per-column power-of-two exponents of X
+  const float* sig;   // [NSB][NB] power-of-two column scales of X per super-block
   unsigned* cnt;      // per-tile super-block counters (zeroed by the X prep)
   float* part;        // [grid][2][NB][128] partial tiles
   float* y;           // y[col * ldy + row]

@@ -9,12 +9,14 @@
 // (dequantize_q4_k, src/quant.rs: d*sc*q - dmin*m per element), where sc, m
 // are 6-bit and q 4-bit integers.  sc*q <= 945 and m <= 63 are integers that
 // fp16 holds exactly, so the decoded tensor-core operand is exact.  Each
-// column of X is scaled by a power of two (its largest magnitude lands in
-// [2^14, 2^15)) and split into fp16 hi + lo (22 significant bits); the group
+// column of X is scaled per super-block by a power of two (its largest
+// magnitude there lands in [2^14, 2^15)) and split into fp16 hi + lo (22
+// significant bits); the group
 // sums enter as sum/32 against 32*m (<= 2016, still exact) so they stay in
 // fp16 range too.  The tensor core sums the exact products in fp32.  Every super-block gets its own fp32
 // accumulators in tensor memory, and the epilogue threads apply d and dmin in
-// fp32 and add the super-blocks in order.
+// fp32, undo the super-block's column scale (exact) and add the super-blocks
+// in order.
 //
 // k_umma_q4k (one CTA per SM, 512 TMEM columns):
 //   warps 0-7   decoders: warp w owns TMEM lanes 32*(w%4).. (one weight row
@@ -206,43 +208,45 @@ __device__ __forceinline__ void raise_timeout(volatile int* abort_flag, uint32_t
 // halves of column n, rows NB + n the lo halves) x 16 fp16, K-major.
 __host__ __device__ constexpr int umma_xtile_bytes(int nb) { return 1088 * nb; }
 
-// Per-column power-of-two scales of X and zeroed tile counters.
-__global__ void k_umma_xscale(const float* __restrict__ x, int cols, long long in_dim, int* __restrict__ xexp,
-                              unsigned* __restrict__ cnt, int tiles) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tiles; i += gridDim.x * blockDim.x) cnt[i] = 0u;
-  __shared__ float red[32];
-  float m = 0.f;
-  const float* xc = x + static_cast<long long>(blockIdx.x) * in_dim;
-  for (long long i = threadIdx.x; i < in_dim; i += blockDim.x) m = fmaxf(m, fabsf(xc[i]));
-  m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 16));
-  m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 8));
-  m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
-  m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
-  m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
-    int e = 0;
-    if (m > 0.f && m <= 3.4e38f) e = ilogbf(m) - 14;  // largest |x| * 2^-e in [2^14, 2^15)
-    xexp[blockIdx.x] = e;
-  }
-  (void)cols;
-}
+// 2^e as a float, exactly (|e| <= 126).
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
-// One super-block s of X per CTA: scaled, permuted to the decoder's K order,
-// split into fp16 hi/lo and laid out as the MMA's K-major B tiles.
+// One super-block s of X per CTA: each column scaled by a power of two (its
+// largest magnitude in the super-block lands in [2^14, 2^15); the inverse goes
+// to sig[s][n] for the epilogue), permuted to the decoder's K order, split into
+// fp16 hi/lo and laid out as the MMA's K-major B tiles.  Also zeroes the tile
+// counters of the launch that follows.
 template <int NB>
 __global__ void __launch_bounds__(256) k_umma_xprep(const float* __restrict__ x, int cols, long long in_dim,
-                                                    const int* __restrict__ xexp, uint8_t* __restrict__ xt) {
-  extern __shared__ float xsm[];  // [NB][257] scaled values, then [NB][8] group sums
+                                                    float* __restrict__ sig, uint8_t* __restrict__ xt,
+                                                    unsigned* __restrict__ cnt, int tiles) {
+  extern __shared__ float xsm[];  // [NB][257] scaled values, then [NB][8] group sums, then [NB] scales
   float* gsum = xsm + NB * 257;
-  const int s = blockIdx.x;
+  float* sinv = gsum + NB * 8;
+  const int s = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tiles; i += gridDim.x * blockDim.x) cnt[i] = 0u;
   for (int i = threadIdx.x; i < NB * 256; i += blockDim.x) {
     const int n = i >> 8, e = i & 255;
-    float v = 0.f;
-    if (n < cols) v = ldexpf(x[static_cast<long long>(n) * in_dim + static_cast<long long>(s) * 256 + e], -xexp[n]);
-    xsm[n * 257 + e] = v;
+    xsm[n * 257 + e] = n < cols ? x[static_cast<long long>(n) * in_dim + static_cast<long long>(s) * 256 + e] : 0.f;
+  }
+  __syncthreads();
+  for (int n = warp; n < NB; n += 8) {
+    float m = 0.f;
+#pragma unroll
+    for (int e = lane; e < 256; e += 32) m = fmaxf(m, fabsf(xsm[n * 257 + e]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    int e = 0;
+    if (m > 0.f && m <= 3.4e38f) e = min(110, max(-110, ilogbf(m) - 14));
+    if (lane == 0) {
+      sinv[n] = pow2f(-e);
+      sig[static_cast<size_t>(s) * NB + n] = pow2f(e);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NB * 256; i += blockDim.x) {
+    const int n = i >> 8, e = i & 255;
+    xsm[n * 257 + e] *= sinv[n];
   }
   __syncthreads();
   for (int i = threadIdx.x; i < NB * 8; i += blockDim.x) {
@@ -463,7 +467,7 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
         if (row < a.rows) {
 #pragma unroll
           for (int c = 0; c < RC; ++c)
-            if (cb + c < a.cols) a.y[static_cast<long long>(cb + c) * a.ldy + row] = ldexpf(acc[c], a.xexp[cb + c]);
+            if (cb + c < a.cols) a.y[static_cast<long long>(cb + c) * a.ldy + row] = acc[c];
         }
       } else {
         const int slot = tile == tile0 ? 0 : 1;
@@ -493,7 +497,7 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
           if (row < a.rows) {
 #pragma unroll
             for (int c = 0; c < RC; ++c)
-              if (cb + c < a.cols) a.y[static_cast<long long>(cb + c) * a.ldy + row] = ldexpf(acc[c], a.xexp[cb + c]);
+              if (cb + c < a.cols) a.y[static_cast<long long>(cb + c) * a.ldy + row] = acc[c];
           }
         }
         named_bar_sync(1, 32 * kRd);  // fin_flag is rewritten by the next piece
@@ -504,6 +508,9 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
 
     for (int kk = 0; kk < K; ++kk) {
       const int db = DB == 2 ? (kk & 1) : 0;
+      float sg[RC];  // column scales of this super-block, fetched before the waits
+#pragma unroll
+      for (int c = 0; c < RC; ++c) sg[c] = __ldg(a.sig + static_cast<size_t>(rs) * NB + cb + c);
       if (!mbar_wait_bounded(&ddfull[kk & 3], (kk >> 2) & 1, kUmmaTimeoutNs, abort_flag) || !wait_sb(kk))
         raise_timeout(abort_flag, a.status);
       const float2 dm = dd[(kk & 3) * kTileRows + r];
@@ -525,7 +532,7 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
           for (int c = 0; c < CH; ++c) {
             const float hl = __uint_as_float(u[c]) + __uint_as_float(v[c]);
             if (ch < C) sm[c] += hl;
-            else acc[c0 + c] += fmaf(dm.x, sm[c], -dm.y * hl);
+            else acc[c0 + c] = fmaf(sg[c0 + c], fmaf(dm.x, sm[c], -dm.y * hl), acc[c0 + c]);
           }
         }
       }
@@ -651,7 +658,8 @@ cudaError_t launch_nb(const UmmaArgs& a, const float* x, long long in_dim, int c
                       int xprep_smem, const CUtensorMap& wmap, cudaStream_t st) {
   cudaError_t e = set_smem<k_umma_xprep<NB>>(xprep_smem);
   if (e != cudaSuccess) return e;
-  k_umma_xprep<NB><<<a.NSB, 256, xprep_smem, st>>>(x, a.cols, in_dim, a.xexp, const_cast<uint8_t*>(a.xt));
+  k_umma_xprep<NB><<<a.NSB, 256, xprep_smem, st>>>(x, a.cols, in_dim, const_cast<float*>(a.sig),
+                                                    const_cast<uint8_t*>(a.xt), a.cnt, a.tiles);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if constexpr (NB == 16) {
     if (chains >= 3) return launch_q4k<16, 3>(a, grid, smem, wmap, st);
@@ -680,10 +688,8 @@ cudaError_t launch_umma_q4k(const UmmaArgs& a, const float* x, long long in_dim,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  const int xprep_smem = (nb * 257 + nb * 8) * 4;
-  k_umma_xscale<<<a.cols, 256, 0, st>>>(x, a.cols, in_dim, const_cast<int*>(a.xexp), a.cnt, a.tiles);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  const int xprep_smem = (nb * 257 + nb * 8 + nb) * 4;
+  cudaError_t e = cudaSuccess;
   switch (nb) {
     case 16: e = launch_nb<16>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
     case 32: e = launch_nb<32>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
