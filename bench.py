@@ -293,7 +293,7 @@ def batched_leg(args, dev) -> dict:
                                 "frac_of_hbm": round(abytes / us / 1e3 / float(peaks["hbm_gbs"]), 4)}
         del gr
     g.close()
-    out["kernel"] = ("k_umma_xscale + k_umma_xprep + k_umma_q4k (tcgen05, up to 64 columns per pass, "
+    out["kernel"] = ("k_umma_xprep + k_umma_q4k (tcgen05, up to 64 columns per pass, "
                      "fp16 sc*q operand in TMEM); B=1 takes k_gemv_mma")
     return out
 
