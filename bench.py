@@ -153,22 +153,13 @@ def cpu_gemv_rate(threads: int, target_s: float, max_calls: int | None = None) -
 DECODE_PROMPT, DECODE_GEN = 128, 256
 
 
-def decode_leg(args, dev, world: int = 1) -> dict:
-    """Greedy decode of the Llama-3.2-1B-shaped model (16 layers, hidden 2048,
-    FFN 8192, 32/8 heads x 64, vocab 128256, Q4_K attention/gate/up/embedding,
-    Q6_K down and head), seeded synthetic weights: a 128-token prompt, then
-    256 generated tokens, all steps device-resident.  Under torchrun the
-    engine is row-sharded over the ranks (FFN and head, NCCL all-gathers) and
-    the time is the max over ranks (strong scaling: one model)."""
+def _decode_run(args, dev, world, shape, tensors, prompt) -> dict:
+    """One decoder: warm-up, then device-timed generation and the e2e call."""
     import torch
     import torch.distributed as dist
 
-    from m3_avm_b200 import model
     from m3_avm_b200.decoder import GpuDecoder
 
-    shape = model.LLAMA_1B
-    tensors = model.synthetic_tensors(shape, seed=1)
-    prompt = model.prompt_tokens(shape, DECODE_PROMPT, seed=2)
     max_pos = DECODE_PROMPT + DECODE_GEN + 8
     if world > 1:
         dec = GpuDecoder.from_torch_dist(shape, max_pos=max_pos, device=dev.index or 0, timeout_s=120)
@@ -198,7 +189,6 @@ def decode_leg(args, dev, world: int = 1) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         gen_ms = float(t.item())
     toks = dec.tokens(DECODE_PROMPT, DECODE_GEN)
-    tok_s = (DECODE_GEN - 1) / (gen_ms / 1e3)
     # e2e: the public call a user makes, host prompt in, host tokens out
     dec.clear_kv_cache()
     if world > 1:
@@ -211,9 +201,40 @@ def decode_leg(args, dev, world: int = 1) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     dec.close()
+    return {"gen_ms": gen_ms, "tok_s": (DECODE_GEN - 1) / (gen_ms / 1e3), "e2e_s": e2e_s, "exchange": exchange,
+            "toks": toks, "match": bool((toks == toks2).all())}
+
+
+def decode_leg(args, dev, world: int = 1) -> dict:
+    """Greedy decode of the Llama-3.2-1B-shaped model (16 layers, hidden 2048,
+    FFN 8192, 32/8 heads x 64, vocab 128256, Q4_K attention/gate/up/embedding,
+    Q6_K down and head), seeded synthetic weights: a 128-token prompt, then
+    256 generated tokens, all steps device-resident.  Under torchrun the engine
+    is row-sharded over the ranks in two ways, both measured: the vocab head
+    alone (every rank keeps the layers; one NCCL all-reduce of the greedy key
+    per token) and the FFN plus the head (rows exchanged every layer); the time
+    is the max over ranks (strong scaling: one model, one sequence)."""
+    from m3_avm_b200 import matvec_quant as MQ
+    from m3_avm_b200 import model
+
+    shape = model.LLAMA_1B
+    tensors = model.synthetic_tensors(shape, seed=1)
+    prompt = model.prompt_tokens(shape, DECODE_PROMPT, seed=2)
+    modes = {}
+    if world > 1:
+        for name, shard_ffn in (("head-only", 0), ("ffn+head", 1)):
+            MQ.set_tuning("decode_shard_ffn", shard_ffn)
+            modes[name] = _decode_run(args, dev, world, shape, tensors, prompt)
+        MQ.set_tuning("decode_shard_ffn", 1)
+        best = max(modes, key=lambda k: modes[k]["tok_s"])
+        r = modes[best]
+    else:
+        r = _decode_run(args, dev, world, shape, tensors, prompt)
+    tok_s, gen_ms, e2e_s = r["tok_s"], r["gen_ms"], r["e2e_s"]
     bytes_tok = shape.weight_bytes_per_token()
     peaks, kind = measured_peaks()
     peak = float(peaks["hbm_gbs"])
+    nccl_per_token = {"nccl": 2 * shape.n_layers + 1, "peer-stores": 0, "head-only": 1, "single": 0}
     out = {
         "workload": "llama-3.2-1b-shaped greedy decode, Q4_K_M mix (Q4_K attn/gate/up/embd, Q6_K down/head)",
         "prompt_tokens": DECODE_PROMPT, "generated_tokens": DECODE_GEN,
@@ -228,17 +249,19 @@ def decode_leg(args, dev, world: int = 1) -> dict:
                        "includes the 128-token prefill)",
                 "h2d_bytes_per_step": 4 * DECODE_PROMPT, "d2h_bytes_per_step": 4 * DECODE_GEN,
                 "seconds": round(e2e_s, 4)},
-        "tokens_match_e2e": bool((toks == toks2).all()),
+        "tokens_match_e2e": r["match"],
         "graph": not args.no_graph,
         "gpu_launches_per_token": 1 + 5 * shape.n_layers + 2,
         "n_gpus": world,
-        "parallelism": f"rows{world} (ffn + head sharded, rows exchanged by {exchange})" if world > 1
-                       else "single GPU",
+        "parallelism": f"rows{world} ({r['exchange']})" if world > 1 else "single GPU",
         "scaling": "strong",
     }
     if world > 1:
-        out["nccl_collectives_per_token"] = 2 * shape.n_layers + 1
+        out["nccl_collectives_per_token"] = nccl_per_token.get(r["exchange"])
         out["roofline"]["note"] = "weight bytes of the whole model per token; each GPU streams its share"
+        out["modes"] = {k: {"tokens_per_s": round(v["tok_s"], 1), "exchange": v["exchange"],
+                            "e2e_tokens_per_s": round(DECODE_GEN / v["e2e_s"], 1)} for k, v in modes.items()}
+        out["modes_tokens_match"] = bool(all((v["toks"] == r["toks"]).all() for v in modes.values()))
     if not args.no_cpu and world == 1:
         out["cpu_baseline"] = cpu_decode_rate(shape, tensors, prompt)
     return out
@@ -648,6 +671,9 @@ def run_decode(args) -> int:
     steps = max(1, min(args.steps, 2048))
     max_pos = DECODE_PROMPT + args.warmup + steps + 8
     if world > 1:
+        from m3_avm_b200 import matvec_quant as MQ
+
+        MQ.set_tuning("decode_shard_ffn", 0 if args.decode_mode == "head-only" else 1)
         dec = GpuDecoder.from_torch_dist(shape, max_pos=max_pos, device=local, timeout_s=120)
     else:
         dec = GpuDecoder(shape, max_pos=max_pos, device=local)
@@ -754,6 +780,8 @@ def main() -> int:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-graph", action="store_true", help="launch each step from the host instead of a CUDA graph")
+    ap.add_argument("--decode-mode", choices=("ffn+head", "head-only"), default="ffn+head",
+                    help="--workload decode under torchrun: rows split over the ranks (FFN and head, or the head)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the 1B decode tokens/s leg")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched Q4_K 28672x8192 sweep")

@@ -92,6 +92,7 @@ struct Tuning {
   int64_t mma_xfirst = 0;         // issue the ring past PRE only once x is loaded
   int64_t decode_xfirst = 0;      // the same for the GEMVs of a decode step
   int64_t decode_p2p = 1;         // sharded decode: peer stores over NVLink instead of NCCL all-gathers
+  int64_t decode_shard_ffn = 1;   // sharded decode: FFN rows split over the ranks (0: only the vocab head)
   int64_t gemm8 = 1;              // batched Q4_K: 8 columns per launch (k_gemm8_q4k) instead of one GEMV each
   int64_t umma = 1;               // batched Q4_K on tcgen05 (k_umma_q4k), up to 64 columns per pass
   int64_t umma_chains = 8;        // independent accumulators per super-block (capped by TMEM)
@@ -635,6 +636,7 @@ int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const flo
 }
 
 bool decode_p2p_enabled() { return g_tune.decode_p2p != 0; }
+bool decode_shard_ffn_enabled() { return g_tune.decode_shard_ffn != 0; }
 
 int status_word(int device, uint32_t** out) {
   DevState* ds = nullptr;
@@ -684,6 +686,7 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "mma_xfirst")) g_tune.mma_xfirst = value != 0;
   else if (!strcmp(key, "decode_xfirst")) g_tune.decode_xfirst = value != 0;
   else if (!strcmp(key, "decode_p2p")) g_tune.decode_p2p = value != 0;
+  else if (!strcmp(key, "decode_shard_ffn")) g_tune.decode_shard_ffn = value != 0;
   else if (!strcmp(key, "gemm8")) g_tune.gemm8 = value != 0;
   else if (!strcmp(key, "umma")) g_tune.umma = value != 0;
   else if (!strcmp(key, "umma_chains") && value >= 1 && value <= 8) g_tune.umma_chains = value;

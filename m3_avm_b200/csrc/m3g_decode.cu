@@ -384,6 +384,7 @@ struct m3g_decoder {
   unsigned int* done = nullptr;  // this rank's finished CTAs, same slots
   int* dstep = nullptr;          // steps completed (advanced by k_pick_step)
   bool p2p = false;
+  bool shard_ffn = false;  // world > 1: FFN rows split too (else every rank keeps the layers, the head is split)
   uint8_t* peer_base[m3g::kMaxPeers] = {};
   int* h_io = nullptr;  // pinned: [0] token / nfixed staging, [1] last token
   uint32_t* status = nullptr;
@@ -449,6 +450,7 @@ void shard_rows(const m3g_decoder* d, int slot, int full_out, int* row0, int* ro
     return;
   }
   const int kind = (slot - kSlotLayer0) % kPerLayer;
+  if (!d->shard_ffn) return;
   if (kind == kGate || kind == kUp) {
     *row0 = d->rank * d->Fr;
     *rows = d->Fr;
@@ -519,7 +521,7 @@ int prepare(m3g_decoder* d) {
     const Tensor* T = &d->t[kSlotLayer0 + kPerLayer * l];
     if (int rc = concat_rows(d, {&T[kQ], &T[kK], &T[kV]}, d->qkv[l])) return rc;
     if (int rc = interleave_gate_up(d, T[kGate], T[kUp], d->gu[l])) return rc;
-    if (d->world > 1 && !d->gu[l].w)
+    if (d->shard_ffn && !d->gu[l].w)
       return host_fail(M3G_EINVAL, "sharded decode needs gate and up of one dtype with 16-byte rows (layer %d)", l);
   }
   d->prepared = true;
@@ -622,7 +624,7 @@ int enqueue_step(m3g_decoder* d) {
       if (int rc = m3g::gemv_fused(d->device, Dn.dtype, Dn.d, Dn.len, d->gub, nullptr, nullptr, yslot, m3g::kXPlain,
                                    yslot, Dn.in, Dn.out, d->st, true, nullptr, false, 0, &dio))
         return rc;
-    } else if (d->world > 1) {  // this rank's rows, then NCCL all-gathers of silu(g) * u and of hidden
+    } else if (d->shard_ffn) {  // this rank's rows, then NCCL all-gathers of silu(g) * u and of hidden
       float* hslot = d->gub + static_cast<size_t>(d->rank) * d->Fr;
       if (int rc = gemv(d, d->gu[l], d->hidden, nullptr, g_ffn, nullptr, m3g::kXRmsNorm, hslot, nullptr, true))
         return rc;
@@ -733,7 +735,9 @@ int check_status(m3g_decoder* d) {
 int setup_peers(m3g_decoder* d) {
   d->p2p = false;
   d->peer_base[d->rank] = d->xregion;
-  if (d->world < 2 || d->world > m3g::kMaxPeers || !m3g::decode_p2p_enabled()) return M3G_OK;
+  // peer stores keep the ranks in step through the per-layer exchanges; with
+  // only the head split, the greedy key is merged by an NCCL all-reduce
+  if (d->world < 2 || d->world > m3g::kMaxPeers || !m3g::decode_p2p_enabled() || !d->shard_ffn) return M3G_OK;
   if (static_cast<long long>(d->cfg.vocab) - static_cast<long long>(d->world - 1) * d->Vr < 1) return M3G_OK;
   constexpr int kRec = 72;  // 64-byte handle + ok flag
   uint8_t rec[kRec] = {};
@@ -831,8 +835,11 @@ M3G_API int m3g_decoder_create_sharded(int device, const m3g_decoder_config* cfg
   *out = nullptr;
   if (world < 1 || rank < 0 || rank >= world) return host_fail(M3G_EINVAL, "rank %d of %d", rank, world);
   if (world > 1 && !nccl_id128) return host_fail(M3G_EINVAL, "sharded decoder needs an NCCL unique id");
-  if (world > 1 && (cfg->ffn % (8ull * world) || cfg->hidden % world || cfg->vocab < static_cast<uint64_t>(world)))
-    return host_fail(M3G_EINVAL, "sharding needs ffn %% (8 * world) == 0 and hidden %% world == 0");
+  const bool shard_ffn = world > 1 && m3g::decode_shard_ffn_enabled();
+  if (world > 1 && cfg->vocab < static_cast<uint64_t>(world))
+    return host_fail(M3G_EINVAL, "sharding needs vocab >= world");
+  if (shard_ffn && (cfg->ffn % (8ull * world) || cfg->hidden % world))
+    return host_fail(M3G_EINVAL, "FFN sharding needs ffn %% (8 * world) == 0 and hidden %% world == 0");
   const m3g_decoder_config& c = *cfg;
   if (!c.n_layers || !c.hidden || !c.ffn || !c.n_heads || !c.n_kv_heads || !c.vocab || !c.max_pos)
     return host_fail(M3G_EINVAL, "zero dimension in the decoder shape");
@@ -854,8 +861,9 @@ M3G_API int m3g_decoder_create_sharded(int device, const m3g_decoder_config* cfg
   d->rank = rank;
   d->world = world;
   d->timeout_s = timeout_s > 0 ? timeout_s : 60.0;
-  d->Fr = static_cast<int>(c.ffn / world);
-  d->hr = static_cast<int>(c.hidden / world);
+  d->shard_ffn = shard_ffn;
+  d->Fr = static_cast<int>(shard_ffn ? c.ffn / world : c.ffn);
+  d->hr = static_cast<int>(shard_ffn ? c.hidden / world : c.hidden);
   d->Vr = static_cast<int>((c.vocab + world - 1) / world);
   d->hd = static_cast<int>(hd);
   d->kvd = static_cast<int>(c.n_kv_heads * hd);
@@ -1064,7 +1072,7 @@ M3G_API const float* m3g_decoder_logits_dev(const m3g_decoder* d) { return d ? d
 
 M3G_API int m3g_decoder_exchange(const m3g_decoder* d) {
   if (!d) return -1;
-  return d->world == 1 ? 0 : (d->p2p ? 2 : 1);
+  return d->world == 1 ? 0 : (!d->shard_ffn ? 3 : (d->p2p ? 2 : 1));
 }
 
 M3G_API void* m3g_decoder_stream(const m3g_decoder* d) { return d ? static_cast<void*>(d->st) : nullptr; }

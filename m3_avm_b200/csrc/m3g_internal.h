@@ -131,6 +131,8 @@ int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const flo
 
 // Whether a sharded decoder may exchange rows by peer stores (tuning knob).
 bool decode_p2p_enabled();
+// Whether a sharded decoder splits the FFN rows too (tuning knob; else only the head).
+bool decode_shard_ffn_enabled();
 
 // The per-device status word the kernels set kStatus* bits in.
 int status_word(int device, uint32_t** out);

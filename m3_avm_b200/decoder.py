@@ -133,7 +133,8 @@ class GpuDecoder:
     @property
     def exchange(self) -> str:
         """'single', 'nccl' or 'peer-stores' (how a sharded engine moves rows)."""
-        return {0: "single", 1: "nccl", 2: "peer-stores"}.get(int(_lib.load().m3g_decoder_exchange(self._h)), "?")
+        return {0: "single", 1: "nccl", 2: "peer-stores", 3: "head-only"}.get(
+            int(_lib.load().m3g_decoder_exchange(self._h)), "?")
 
     @property
     def logits_ptr(self) -> int:

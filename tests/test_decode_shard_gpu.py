@@ -1,9 +1,10 @@
 """Sharded decode (one process per GPU, NCCL) against the single-GPU engine.
 
-Each rank keeps its rows of ffn_gate/up/down and the vocab head; every row
-is computed exactly as on one GPU, so the sharded steps must reproduce the
-single-GPU logits and greedy tokens bit for bit -- with the rows exchanged by
-peer stores from the GEMV epilogues, and with NCCL all-gathers.  Also: a rank that never
+Each rank keeps its rows of ffn_gate/up/down and the vocab head (or only of
+the head, every rank keeping the layers); every row is computed exactly as on
+one GPU, so the sharded steps must reproduce the single-GPU logits and greedy
+tokens bit for bit -- with the rows exchanged by peer stores from the GEMV
+epilogues, with NCCL all-gathers, and with the head split alone.  Also: a rank that never
 joins makes creation give up with M3G_ETIMEOUT (host-side failure detection,
 nothing waits on the GPU).
 """
@@ -23,11 +24,12 @@ PROMPT = [5, 77, 1000, 4098, 3]
 N_GEN = 6
 
 
-def _run(shape, rank, world, uid, p2p=1):
+def _run(shape, rank, world, uid, p2p=1, shard_ffn=1):
     from m3_avm_b200 import matvec_quant as MQ
     from m3_avm_b200.decoder import GpuDecoder
 
     MQ.set_tuning("decode_p2p", p2p)
+    MQ.set_tuning("decode_shard_ffn", shard_ffn)
 
     d = GpuDecoder(shape, max_pos=32, device=rank, rank=rank, world=world, nccl_id=uid, timeout_s=60)
     d.upload_all(model.synthetic_tensors(shape, 3))
@@ -38,19 +40,19 @@ def _run(shape, rank, world, uid, p2p=1):
     return [lg.tobytes() for lg in logits], toks.tobytes()
 
 
-def _rank(rank, world, uid, p2p, q):
+def _rank(rank, world, uid, p2p, shard_ffn, q):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     import torch
 
     torch.cuda.set_device(rank)
     try:
-        q.put((rank, _run(SHAPE, rank, world, uid, p2p)))
+        q.put((rank, _run(SHAPE, rank, world, uid, p2p, shard_ffn)))
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, repr(e)))
 
 
-@pytest.mark.parametrize("p2p", [1, 0], ids=["peer-stores", "nccl"])
-def test_sharded_decode_matches_single_gpu_bitwise(p2p):
+@pytest.mark.parametrize("p2p,shard_ffn", [(1, 1), (0, 1), (1, 0)], ids=["peer-stores", "nccl", "head-only"])
+def test_sharded_decode_matches_single_gpu_bitwise(p2p, shard_ffn):
     import multiprocessing as mp
 
     import torch
@@ -63,7 +65,7 @@ def test_sharded_decode_matches_single_gpu_bitwise(p2p):
     uid = sharded.unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, uid, p2p, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, p2p, shard_ffn, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=120) for _ in range(world))
