@@ -80,7 +80,7 @@ struct Tuning {
   int64_t pdl = 1;              // programmatic dependent launch of the streaming kernels
   int64_t mma = 1;              // tensor-core GEMV where the shape allows it
   int64_t mma_stages = 5;       // pipeline stages of the tensor-core GEMV
-  int64_t mma_tps = 1;          // 16-row tiles per stage (1: 8 consumer warps, 2: 16)
+  int64_t mma_tps = 0;          // 16-row tiles per stage of 8-warp tiles (1, 2; 0: 2 for long runs of short rows)
   int64_t mma_kc = 16;          // super-blocks per k-chunk (<= 16)
   int64_t mma_ctas = 1;         // CTAs per SM the tensor-core GEMV is sized for
   int64_t mma_wk = 0;           // consumer warps splitting a tile's k-chunk (8, 16; 0 = by shape)
@@ -233,7 +233,13 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   // for the heavier Q6_K decode; 8 otherwise.  mma_wk = 8 / 16 forces it.
   int wk = g_tune.mma_wk;
   if (wk != 8 && wk != 16) wk = ((NSB == 16 && KC == 16) || (f.fmt == 14 && NSB >= 16)) ? 16 : 8;
-  const int tps = wk == 16 ? 1 : static_cast<int>(std::min<int64_t>(2, std::max<int64_t>(1, g_tune.mma_tps)));
+  // Two 8-warp tiles per stage (16 consumer warps) pay off when each CTA
+  // streams many short rows (measured: Q6_K 128256x2048 -31 %, Q4_K
+  // 16384x2048 -10 %) and cost on small or long-row shapes (2048x2048 +19 %,
+  // 28672x8192 +3 %).
+  const long long rows_per_sm = (rows + ds.sms - 1) / ds.sms;
+  const int auto_tps = NSB <= 8 && rows_per_sm >= 64 ? 2 : 1;
+  const int tps = wk == 16 ? 1 : (g_tune.mma_tps == 0 ? auto_tps : static_cast<int>(std::min<int64_t>(2, g_tune.mma_tps)));
   if (f.fmt == 14) {  // 210-byte blocks: chunk sizes must stay multiples of 16 bytes
     if (NSB % 8) return false;
     KC = std::max<long long>(8, KC / 8 * 8);
@@ -550,7 +556,7 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
                const float* gamma, const float* res, int xmode, float* y, long long in_dim, long long out_dim,
                cudaStream_t st, bool decode, unsigned long long* argmax_key, bool swiglu, long long key_row0,
                const PeerIO* peers, int* grid_out) {
-  const bool coresident = decode && g_tune.decode_coresident;
+  bool coresident = decode && g_tune.decode_coresident;
   if (swiglu && (out_dim % 16 || xmode == kXSiluMul || res || argmax_key))
     return fail(M3G_EINVAL, "SwiGLU epilogue needs gate/up rows in 16-row blocks and no other epilogue");
   FmtInfo f;
@@ -561,6 +567,10 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
   if (gamma && reinterpret_cast<uintptr_t>(gamma) % 16) return fail(M3G_EINVAL, "norm weights not 16-byte aligned");
   DevState* ds = nullptr;
   if (int rc = dev_state(device, &ds)) return rc;
+  // Half-SM CTAs let the next small GEMV start beside this one; a GEMV with
+  // many rows per SM (the FFN gate|up, the vocab head) runs long enough to
+  // prefer whole SMs and the deeper pipeline that goes with them.
+  if (coresident && (out_dim + ds->sms - 1) / ds->sms >= 64) coresident = false;
   MmaPlan mp;
   // A half-SM CTA needs two stages of the row segment; wide Q6_K rows may not
   // fit, and then the CTA takes the whole SM.
@@ -674,7 +684,7 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "pdl")) g_tune.pdl = value != 0;
   else if (!strcmp(key, "mma")) g_tune.mma = value != 0;
   else if (!strcmp(key, "mma_stages") && value >= 2 && value <= 8) g_tune.mma_stages = value;
-  else if (!strcmp(key, "mma_tps") && value >= 1 && value <= 2) g_tune.mma_tps = value;
+  else if (!strcmp(key, "mma_tps") && value >= 0 && value <= 2) g_tune.mma_tps = value;
   else if (!strcmp(key, "mma_kc") && value >= 1 && value <= 16) g_tune.mma_kc = value;
   else if (!strcmp(key, "mma_ctas") && value >= 1 && value <= 2) g_tune.mma_ctas = value;
   else if (!strcmp(key, "mma_wk") && (value == 0 || value == 8 || value == 16)) g_tune.mma_wk = value;
