@@ -105,20 +105,50 @@ __global__ void __launch_bounds__(kAttnSplitThreads) k_attention_split(const Att
   const int rank = static_cast<int>(cluster.block_rank());
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hh = blockIdx.x / kAttnSplit, kv = hh / a.groups;
-  grid_dep_wait();
-  grid_dep_launch();
+  // The position, its RoPE row and the cached K/V rows before it were written
+  // by kernels that completed before this step's q|k|v GEMV began, so they are
+  // loaded (into registers) before that GEMV -- the grid dependency -- ends.
   const int pos = *a.pos;
   const bool pos_ok = pos >= 0 && pos < a.max_pos;
-  if (!pos_ok && tid == 0 && rank == 0 && hh == 0) atomicOr(a.status, kStatusBadPos);
   const int npos = pos_ok ? pos + 1 : 0;
   const int chunk = (npos + kAttnSplit - 1) / kAttnSplit;
   const int i0 = min(npos, rank * chunk), i1 = min(npos, i0 + chunk);
+  const int ic = min(i1, pos);  // cached rows are i0 .. ic-1
+  constexpr bool kPre = HD == 64;
+  constexpr int VP = kPre ? 16 : 1;  // V rows per warp held in registers
+  float4 kreg[kPre ? HD / 4 : 1];
+  float vreg[VP][DPL];
+  const bool kpre = kPre && i0 + tid < ic;
+  if (kpre) {
+    const float4* kr = reinterpret_cast<const float4*>(a.kc + static_cast<size_t>(i0 + tid) * a.kvd + kv * HD);
+#pragma unroll
+    for (int j = 0; j < (kPre ? HD / 4 : 1); ++j) kreg[j] = kr[j];
+  }
+  if (kPre) {
+#pragma unroll
+    for (int j = 0; j < VP; ++j) {
+      const int i = i0 + warp + NW * j;
+      if (i < ic) {
+        const float* vr = a.vc + static_cast<size_t>(i) * a.kvd + kv * HD + DPL * lane;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) vreg[j][d] = vr[d];
+      }
+    }
+  }
+  float cs_c = 0.f, cs_s = 0.f;
+  if (pos_ok && tid < HALF) {
+    cs_c = a.rope[static_cast<size_t>(pos) * HD + 2 * tid];
+    cs_s = a.rope[static_cast<size_t>(pos) * HD + 2 * tid + 1];
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  if (!pos_ok && tid == 0 && rank == 0 && hh == 0) atomicOr(a.status, kStatusBadPos);
   if (pos_ok) {
-    const float* cs = a.rope + static_cast<size_t>(pos) * HD;
     const float* q = a.qkv + hh * HD;
     const float* k = a.qkv + a.qd + kv * HD;
+    static_assert(HALF <= kAttnSplitThreads, "one RoPE pair per thread");
     for (int i = tid; i < HALF; i += kAttnSplitThreads) {
-      const float c = cs[2 * i], s = cs[2 * i + 1];
+      const float c = cs_c, s = cs_s;
       float x0 = q[i], x1 = q[i + HALF];
       qs[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
       qs[i + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
@@ -139,10 +169,11 @@ __global__ void __launch_bounds__(kAttnSplitThreads) k_attention_split(const Att
   float lmax = -INFINITY;
   for (int i = i0 + tid; i < i1; i += kAttnSplitThreads) {
     const float* kr = i == pos ? kn : a.kc + static_cast<size_t>(i) * a.kvd + kv * HD;
+    const bool inreg = kpre && i == i0 + tid;
     float dot = 0.f;
 #pragma unroll
     for (int j = 0; j < HD; j += 4) {
-      const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+      const float4 k4 = inreg ? kreg[kPre ? j / 4 : 0] : *reinterpret_cast<const float4*>(kr + j);
       const float4 q4 = *reinterpret_cast<const float4*>(qs + j);
       dot = __fadd_rn(dot, __fmul_rn(q4.x, k4.x));
       dot = __fadd_rn(dot, __fmul_rn(q4.y, k4.y));
@@ -172,8 +203,21 @@ __global__ void __launch_bounds__(kAttnSplitThreads) k_attention_split(const Att
   float acc[DPL];
 #pragma unroll
   for (int d = 0; d < DPL; ++d) acc[d] = 0.f;
+  int vfirst = i0 + warp;  // rows still to read from memory start here
+  if (kPre) {
+#pragma unroll
+    for (int j = 0; j < VP; ++j) {
+      const int i = i0 + warp + NW * j;
+      if (i < ic) {
+        const float w = sc[i - i0];
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) acc[d] += w * vreg[j][d];
+        vfirst = i + NW;
+      }
+    }
+  }
 #pragma unroll 4
-  for (int i = i0 + warp; i < i1; i += NW) {
+  for (int i = vfirst; i < i1; i += NW) {
     const float w = sc[i - i0];
     const float* vr = (i == pos ? vn : a.vc + static_cast<size_t>(i) * a.kvd + kv * HD) + DPL * lane;
     if (DPL == 2) {
