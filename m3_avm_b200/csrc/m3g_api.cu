@@ -96,6 +96,7 @@ struct Tuning {
   int64_t gemm8 = 1;              // batched Q4_K: 8 columns per launch (k_gemm8_q4k) instead of one GEMV each
   int64_t umma = 1;               // batched Q4_K on tcgen05 (k_umma_q4k), up to 64 columns per pass
   int64_t umma_chains = 8;        // independent accumulators per super-block (capped by TMEM)
+  int64_t offload_graph = 1;      // host-buffer offload calls replay one CUDA graph (copy in, GEMV, copy out)
 };
 Tuning g_tune;
 
@@ -699,6 +700,7 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "decode_shard_ffn")) g_tune.decode_shard_ffn = value != 0;
   else if (!strcmp(key, "gemm8")) g_tune.gemm8 = value != 0;
   else if (!strcmp(key, "umma")) g_tune.umma = value != 0;
+  else if (!strcmp(key, "offload_graph")) g_tune.offload_graph = value != 0;
   else if (!strcmp(key, "umma_chains") && value >= 1 && value <= 8) g_tune.umma_chains = value;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
@@ -962,6 +964,16 @@ struct m3g_offload {
   uint32_t* h_status = nullptr;
   uint64_t calls = 0;
   std::unordered_map<uint64_t, ResidentTensor> tensors;
+  // Host-buffer calls: one captured graph per tensor (copy x in, GEMV, copy y
+  // and the status word out), valid for the batch, weight and staging
+  // buffers it was captured with.
+  struct HostGraph {
+    cudaGraphExec_t exec = nullptr;
+    uint64_t batch = 0;
+    const uint8_t* w = nullptr;
+  };
+  std::unordered_map<uint64_t, HostGraph> graphs;
+  bool graphs_ok = true;  // cleared if a capture ever fails: calls then run eagerly
 };
 
 namespace {
@@ -977,7 +989,14 @@ struct DeviceGuard {
   }
 };
 
+void drop_graphs(m3g_offload* c) {
+  for (auto& kv : c->graphs)
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+  c->graphs.clear();
+}
+
 void free_io(m3g_offload* c) {
+  drop_graphs(c);
   if (c->d_x) cudaFree(c->d_x);
   if (c->d_y) cudaFree(c->d_y);
   if (c->h_x) cudaFreeHost(c->h_x);
@@ -1036,6 +1055,7 @@ void m3g_offload_destroy(m3g_offload* c) {
   if (!c) return;
   DeviceGuard g(c->device);
   cudaDeviceSynchronize();
+  drop_graphs(c);
   for (auto& kv : c->tensors) cudaFree(kv.second.d_raw);
   free_io(c);
   cudaStreamDestroy(c->stream);
@@ -1070,6 +1090,11 @@ int m3g_offload_upload(m3g_offload* c, uint64_t tidx, uint32_t dtype, const uint
   auto it = c->tensors.find(tidx);
   if (it != c->tensors.end()) {
     cudaDeviceSynchronize();  // the old bytes may be in use on any stream
+    auto gi = c->graphs.find(tidx);
+    if (gi != c->graphs.end()) {
+      if (gi->second.exec) cudaGraphExecDestroy(gi->second.exec);
+      c->graphs.erase(gi);
+    }
     cudaFree(it->second.d_raw);
     it->second = t;
   } else {
@@ -1127,12 +1152,50 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
   const size_t bx = static_cast<size_t>(in_dim * batch) * sizeof(float);
   const size_t by = static_cast<size_t>(out_dim * batch) * sizeof(float);
   memcpy(c->h_x, x, bx);
-  M3G_CUDA(cudaMemcpyAsync(c->d_x, c->h_x, bx, cudaMemcpyHostToDevice, c->stream));
-  if (int rc = m3g_offload_matvec_dev(c, tidx, c->d_x, batch, c->d_y, c->stream)) return rc;
   DevState* ds = nullptr;
   if (int rc = dev_state(c->device, &ds)) return rc;
-  M3G_CUDA(cudaMemcpyAsync(c->h_y, c->d_y, by, cudaMemcpyDeviceToHost, c->stream));
-  M3G_CUDA(cudaMemcpyAsync(c->h_status, ds->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+  // copy in, GEMV, copy out and the status word, on c->stream
+  auto enqueue = [&]() -> int {
+    M3G_CUDA(cudaMemcpyAsync(c->d_x, c->h_x, bx, cudaMemcpyHostToDevice, c->stream));
+    if (int rc = m3g_offload_matvec_dev(c, tidx, c->d_x, batch, c->d_y, c->stream)) return rc;
+    M3G_CUDA(cudaMemcpyAsync(c->h_y, c->d_y, by, cudaMemcpyDeviceToHost, c->stream));
+    M3G_CUDA(cudaMemcpyAsync(c->h_status, ds->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+    return M3G_OK;
+  };
+  m3g_offload::HostGraph* hg = nullptr;
+  if (g_tune.offload_graph && c->graphs_ok) {
+    auto gi = c->graphs.find(tidx);
+    if (gi != c->graphs.end() && (gi->second.batch != batch || gi->second.w != t.d_raw)) {
+      if (gi->second.exec) cudaGraphExecDestroy(gi->second.exec);
+      c->graphs.erase(gi);
+      gi = c->graphs.end();
+    }
+    if (gi == c->graphs.end()) {
+      cudaGraph_t graph = nullptr;
+      cudaGraphExec_t exec = nullptr;
+      const uint64_t calls0 = c->calls;  // capturing is not a call
+      bool ok = cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+      const int rc = ok ? enqueue() : M3G_OK;
+      c->calls = calls0;
+      ok = (cudaStreamEndCapture(c->stream, &graph) == cudaSuccess) && ok && rc == M3G_OK;
+      if (ok) ok = cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+      if (graph) cudaGraphDestroy(graph);
+      cudaGetLastError();  // a failed capture leaves no sticky error; clear the last one
+      if (ok) {
+        gi = c->graphs.emplace(tidx, m3g_offload::HostGraph{exec, batch, t.d_raw}).first;
+      } else {
+        if (exec) cudaGraphExecDestroy(exec);
+        c->graphs_ok = false;  // run this and later calls eagerly
+      }
+    }
+    if (gi != c->graphs.end()) hg = &gi->second;
+  }
+  if (hg) {
+    M3G_CUDA(cudaGraphLaunch(hg->exec, c->stream));
+    ++c->calls;
+  } else if (int rc = enqueue()) {
+    return rc;
+  }
   M3G_CUDA(cudaStreamSynchronize(c->stream));
   memcpy(y, c->h_y, by);
   if (*c->h_status & m3g::kStatusCopyTimeout) {
