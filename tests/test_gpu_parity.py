@@ -367,3 +367,33 @@ def test_gemm8_equals_per_column_gemv(m3):
     for k in range(batch):
         bound = gemv_bound(raw, 12, in_dim, out_dim, X[k])
         assert np.all(np.abs(a[k].cpu().numpy().astype(np.float64) - b[k].cpu().numpy()) <= 2 * bound)
+
+
+def test_offload_replayed_calls_follow_reuploads_and_batch_sizes(m3):
+    """Host-buffer offload calls replay a captured graph per tensor: a new
+    upload of the same index, a different batch and a larger staging buffer
+    must each give the oracle's result for the current weights."""
+    g = m3.inference_gpu.GpuOffload.try_new(4096, 1024)
+    assert g is not None
+    raw_a = m3.synth.weights(12, 4096, 1024, seed=61)
+    raw_b = m3.synth.weights(12, 4096, 1024, seed=62)
+    x = m3.synth.activations(4096, seed=63)
+    assert g.upload(3, 12, raw_a, 4096, 1024)
+    for _ in range(2):  # the second call replays the graph
+        check_gemv(g.matvec(3, x, 4096, 1024), raw_a, 12, 4096, 1024, x)
+    assert g.upload(3, 12, raw_b, 4096, 1024)  # same index, new weights
+    for _ in range(2):
+        check_gemv(g.matvec(3, x, 4096, 1024), raw_b, 12, 4096, 1024, x)
+    X = m3.synth.activations(4096, seed=64, batch=5)  # larger staging buffers, batched path
+    Y = g.matvec_batch(3, X, 4096, 1024)
+    for b in range(5):
+        check_gemv(Y[b], raw_b, 12, 4096, 1024, X[b])
+    x2 = m3.synth.activations(4096, seed=65)  # back to one column, new x
+    check_gemv(g.matvec(3, x2, 4096, 1024), raw_b, 12, 4096, 1024, x2)
+    assert g.calls == 6
+    m3.matvec_quant.set_tuning("offload_graph", 0)
+    try:
+        check_gemv(g.matvec(3, x2, 4096, 1024), raw_b, 12, 4096, 1024, x2)
+    finally:
+        m3.matvec_quant.set_tuning("offload_graph", 1)
+    g.close()
