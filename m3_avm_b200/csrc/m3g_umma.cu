@@ -11,35 +11,36 @@
 // fp16 holds exactly, so the decoded tensor-core operand is exact.  Each
 // column of X is scaled per super-block by a power of two (its largest
 // magnitude there lands in [2^14, 2^15)) and split into fp16 hi + lo (22
-// significant bits); the group
-// sums enter as sum/32 against 32*m (<= 2016, still exact) so they stay in
-// fp16 range too.  The tensor core sums the exact products in fp32.  Every super-block gets its own fp32
-// accumulators in tensor memory, and the epilogue threads apply d and dmin in
-// fp32, undo the super-block's column scale (exact) and add the super-blocks
-// in order.
+// significant bits); the group sums enter as sum/32 against 32*m (<= 2016,
+// still exact) so they stay in fp16 range too.  The tensor core sums the
+// exact products in fp32.  Every super-block gets its own fp32 accumulators
+// in tensor memory, and the readout threads apply d and dmin in fp32, undo
+// the super-block's column scale (exact) and add the super-blocks in order.
 //
-// k_umma_q4k (one CTA per SM, 512 TMEM columns):
-//   warps 0-7   decoders: warp w owns TMEM lanes 32*(w%4).. (one weight row
-//               per thread) and half w/4 of the super-block; they decode the
-//               4-bit quants straight into tensor memory (tcgen05.st, the A
-//               operand), the m values into shared memory and (d, dmin) into a
-//               shared ring;
-//   warps 8-11  readout: warp 8+q reads lanes 32q.. of the super-block's
-//               accumulators back (tcgen05.ld), applies d and dmin and keeps
-//               the per-row fp32 sums, and writes finished tiles;
-//   warp 12     producer: per super-block, one 2-D tensor copy of the 128-row
+// k_umma_q4k<NB, C> (one CTA per SM, 512 TMEM columns; D = 16 decoder warps
+// for NB = 16, 8 otherwise; R = 4 readout warps, 8 for NB = 64):
+//   decoders    warp w owns TMEM lanes 32*(w%4).. (one weight row per
+//               thread) and part w/4 of the super-block's quants; they decode
+//               the 4-bit quants straight into tensor memory (tcgen05.st, the
+//               A operand), the m values into shared memory and (d, dmin) into
+//               a shared ring;
+//   readout     warp D+r reads lanes 32*(r%4).. of the super-block's
+//               accumulators back (tcgen05.ld; two warps per quarter split the
+//               columns), applies d, dmin and the column scale, keeps the
+//               per-row fp32 sums and writes finished tiles;
+//   producer    warp D+R: per super-block, one 2-D tensor copy of the 128-row
 //               weight tile (a box of 36 words x 128 rows of the row-major
-//               Q4_K matrix; rows past the end read as zero) and one bulk copy
-//               of the prepared X tile;
-//   warps 13..12+C  MMA issuers (warp 13 also allocates TMEM): lane 0 of
-//               issuer c issues the K-steps t = c, c + C, ... of each
-//               super-block (M = 128, N = 2*NB, K = 16): sc*q (TMEM) x
-//               [X hi | X lo] (shared) into main accumulator c; issuer 0 also
-//               issues m (shared) x [group sums hi | lo] into the min
-//               accumulator; each commits to the stage's mbarriers.  An MMA
-//               costs an issuing warp about as much at N = 32 as at N = 128
-//               and several issuing warps proceed in parallel, so the hi and lo
-//               halves of X share one instruction and C warps issue.
+//               Q4_K matrix; rows past the end read as zero) and one bulk
+//               copy of the prepared X tile;
+//   issuers     C warps (the first also allocates TMEM): lane 0 of issuer c
+//               issues the K-steps t = c, c + C, ... of each super-block
+//               (M = 128, N = 2*NB, K = 16): sc*q (TMEM) x [X hi | X lo]
+//               (shared) into main accumulator c; the last issuer also issues
+//               m (shared) x [group sums hi | lo] into the min accumulator;
+//               each commits once per super-block.  An MMA costs an issuing
+//               warp about as much at N = 32 as at N = 128 and several issuing
+//               warps proceed in parallel, so the hi and lo halves of X share
+//               one instruction and C warps issue.
 // The (tile, super-block) iteration space is split evenly over the CTAs; a
 // tile cut between CTAs is finished by the CTA whose piece completes it, which
 // adds the pieces in CTA order (the result does not depend on timing).
@@ -134,21 +135,6 @@ __device__ __forceinline__ void tc_ld2x8(uint32_t ta, uint32_t tb, uint32_t (&x)
       : "r"(ta), "r"(tb)
       : "memory");
 }
-__device__ __forceinline__ void tc_ld2x16(uint32_t ta, uint32_t tb, uint32_t (&x)[16], uint32_t (&y)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%32];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
-      "%29, %30, %31}, [%33];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]), "=r"(x[6]), "=r"(x[7]), "=r"(x[8]),
-        "=r"(x[9]), "=r"(x[10]), "=r"(x[11]), "=r"(x[12]), "=r"(x[13]), "=r"(x[14]), "=r"(x[15]), "=r"(y[0]),
-        "=r"(y[1]), "=r"(y[2]), "=r"(y[3]), "=r"(y[4]), "=r"(y[5]), "=r"(y[6]), "=r"(y[7]), "=r"(y[8]), "=r"(y[9]),
-        "=r"(y[10]), "=r"(y[11]), "=r"(y[12]), "=r"(y[13]), "=r"(y[14]), "=r"(y[15])
-      : "r"(ta), "r"(tb)
-      : "memory");
-}
-
 // Shared-memory matrix descriptor, K-major, no swizzle: 8-row x 16-byte core
 // matrices, `lbo` bytes between the two core matrices along K, `sbo` bytes
 // between 8-row groups; descriptor version 1, base offset 0.
@@ -312,7 +298,8 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
   constexpr int DB = 256 + 2 * (C + 1) * DW <= static_cast<int>(kTmemCols) ? 2 : 1;  // accumulator buffers
   static_assert(256 + DB * (C + 1) * DW <= static_cast<int>(kTmemCols), "TMEM columns");
   constexpr uint32_t XS = umma_xtile_bytes(NB);
-  constexpr int CH = RC <= 32 ? 8 : 16;  // accumulator columns per tcgen05.ld
+  constexpr int CH = 8;  // accumulator columns per tcgen05.ld
+  static_assert(RC % CH == 0, "readout columns");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long G = gridDim.x;
   const long long it0 = static_cast<long long>(blockIdx.x) * a.T / G;
@@ -526,8 +513,7 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
         for (int ch = 0; ch <= C; ++ch) {  // C main accumulators, then the min accumulator
           uint32_t u[CH], v[CH];
           const uint32_t ta = dbase + static_cast<uint32_t>(ch * DW + c0);
-          if constexpr (CH == 8) tc_ld2x8(ta, ta + NB, u, v);  // hi and lo halves of columns c0..
-          else tc_ld2x16(ta, ta + NB, u, v);
+          tc_ld2x8(ta, ta + NB, u, v);  // hi and lo halves of columns c0..c0+7
 #pragma unroll
           for (int c = 0; c < CH; ++c) {
             const float hl = __uint_as_float(u[c]) + __uint_as_float(v[c]);
