@@ -400,7 +400,7 @@ bool plan_umma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t
                const DevState& ds, UmmaPlan& p) {
   if (f.fmt != 12 || in_dim % 256 || in_dim > (1 << 22) || cols < 1 || cols > 64) return false;
   if (reinterpret_cast<uintptr_t>(w) % 16 || rows < 1 || rows > (1ll << 31) - 1) return false;
-  const int nb = cols <= 16 ? 16 : cols <= 32 ? 32 : 64;
+  const int nb = cols <= 8 ? 8 : cols <= 16 ? 16 : cols <= 32 ? 32 : 64;
   const long long XS = m3g::umma_xtile(nb), SW = 128 * 144;
   const long long avail = std::min<long long>(ds.smem_optin, 232448) - 8192 - 4096 - 256;
   long long NSX = 0, NSW = 0;

@@ -151,8 +151,8 @@ struct Gemm8Args {
 cudaError_t launch_xprep8(const float* x, int cols, int in_dim, uint8_t* out, cudaStream_t st);
 cudaError_t launch_gemm8_q4k(const Gemm8Args& a, int grid, size_t smem, cudaStream_t st);
 
-// Batched Q4_K on tcgen05 (m3g_umma.cu): up to 64 columns per pass, NB = 16,
-// 32 or 64 accumulator columns, 128-row tiles split evenly over the CTAs.
+// Batched Q4_K on tcgen05 (m3g_umma.cu): up to 64 columns per pass, NB = 8,
+// 16, 32 or 64 accumulator columns, 128-row tiles split evenly over the CTAs.
 struct UmmaArgs {
   const uint8_t* w;   // Q4_K rows, RB bytes apart
   const uint8_t* xt;  // prepared X tiles, umma_xtile(NB) bytes per super-block

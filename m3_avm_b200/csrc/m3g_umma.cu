@@ -17,8 +17,9 @@
 // in tensor memory, and the readout threads apply d and dmin in fp32, undo
 // the super-block's column scale (exact) and add the super-blocks in order.
 //
-// k_umma_q4k<NB, C> (one CTA per SM, 512 TMEM columns; D = 16 decoder warps
-// for NB = 16, 8 otherwise; R = 4 readout warps, 8 for NB = 64):
+// k_umma_q4k<NB, C> (NB = 8, 16, 32 or 64; one CTA per SM, 512 TMEM columns;
+// D = 16 decoder warps for NB <= 16, 8 otherwise; R = 4 readout warps, 8 for
+// NB = 64):
 //   decoders    warp w owns TMEM lanes 32*(w%4).. (one weight row per
 //               thread) and part w/4 of the super-block's quants; they decode
 //               the 4-bit quants straight into tensor memory (tcgen05.st, the
@@ -647,7 +648,11 @@ cudaError_t launch_nb(const UmmaArgs& a, const float* x, long long in_dim, int c
   k_umma_xprep<NB><<<a.NSB, 256, xprep_smem, st>>>(x, a.cols, in_dim, const_cast<float*>(a.sig),
                                                     const_cast<uint8_t*>(a.xt), a.cnt, a.tiles);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  if constexpr (NB == 16) {
+  if constexpr (NB == 8) {
+    if (chains >= 3) return launch_q4k<8, 3>(a, grid, smem, wmap, st);
+    if (chains >= 2) return launch_q4k<8, 2>(a, grid, smem, wmap, st);
+    return launch_q4k<8, 1>(a, grid, smem, wmap, st);
+  } else if constexpr (NB == 16) {
     if (chains >= 3) return launch_q4k<16, 3>(a, grid, smem, wmap, st);
     if (chains >= 2) return launch_q4k<16, 2>(a, grid, smem, wmap, st);
     return launch_q4k<16, 1>(a, grid, smem, wmap, st);
@@ -677,6 +682,7 @@ cudaError_t launch_umma_q4k(const UmmaArgs& a, const float* x, long long in_dim,
   const int xprep_smem = (nb * 257 + nb * 8 + nb) * 4;
   cudaError_t e = cudaSuccess;
   switch (nb) {
+    case 8: e = launch_nb<8>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
     case 16: e = launch_nb<16>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
     case 32: e = launch_nb<32>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
     case 64: e = launch_nb<64>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
