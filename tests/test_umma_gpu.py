@@ -5,7 +5,7 @@ oracle's fp32 result, at shapes that reach each part of the kernel:
 * tiles cut between CTAs (one super-block per CTA; pieces finished by the
   CTA that completes the tile) and CTAs spanning several tiles;
 * a ragged last tile (rows % 128 != 0), a single super-block per row;
-* 16, 32 and 64 accumulator columns, and more than 64 columns (two passes);
+* 8, 16, 32 and 64 accumulator columns, and more than 64 columns (two passes);
 * columns of very different magnitudes and an all-zero column (the
   per-column power-of-two scaling of X);
 * the batched-decode weight 28672 x 8192 at B = 16.
