@@ -459,7 +459,7 @@ def run_ours(args) -> int:
             graphs.append((n_launch, gr))
     gmap = dict(graphs)
 
-    def run_steps(k):
+    def run_steps(k, marks=None):
         if args.no_graph:
             for i in range(k):
                 step(i, stream)
@@ -467,6 +467,10 @@ def run_ours(args) -> int:
         full, rest = divmod(k, n_copies)
         for _ in range(full):
             gmap[n_copies].replay()
+            if marks is not None:  # window boundaries: the median and best window are reported too
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(stream)
+                marks.append(ev)
         if rest:
             if rest not in gmap:
                 for i in range(rest):
@@ -484,10 +488,14 @@ def run_ours(args) -> int:
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    run_steps(args.steps)
+    marks = [ev0]
+    run_steps(args.steps, marks)
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     host_launches = int(lib.m3g_launch_count()) - launches0
+    win_us = [a.elapsed_time(b) * 1e3 / n_copies for a, b in zip(marks, marks[1:])]
+    windows = ({"median_us": round(statistics.median(win_us), 3), "best_us": round(min(win_us), 3),
+                "windows": len(win_us), "steps_per_window": n_copies} if win_us else None)
     launches = args.steps if not args.no_graph else host_launches
     ms = ev0.elapsed_time(ev1)
     barrier()
@@ -555,6 +563,7 @@ def run_ours(args) -> int:
                     "d2h_bytes_per_step": 4 * OUT_DIM, "us_per_call": round(float(te.item()) * 1e6, 2),
                     "api": "m3g_offload_matvec (host x/y, resident weights)"},
             "gpu_launches": launches,
+            "per_step_windows": windows,
             "timing": "CUDA events around CUDA-graph replays of the GEMV launches" if not args.no_graph
                       else "CUDA events around host-launched GEMVs",
             "clocks": clocks,
