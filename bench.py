@@ -211,9 +211,10 @@ def decode_leg(args, dev, world: int = 1) -> dict:
     Q6_K down and head), seeded synthetic weights: a 128-token prompt, then
     256 generated tokens, all steps device-resident.  Under torchrun the engine
     is row-sharded over the ranks in two ways, both measured: the vocab head
-    alone (every rank keeps the layers; one NCCL all-reduce of the greedy key
-    per token) and the FFN plus the head (rows exchanged every layer); the time
-    is the max over ranks (strong scaling: one model, one sequence)."""
+    alone (every rank keeps the layers; the greedy keys merge by peer atomics
+    over NVLink, or by one NCCL all-reduce per token where peers cannot be
+    mapped) and the FFN plus the head (rows exchanged every layer); the time is
+    the max over ranks (strong scaling: one model, one sequence)."""
     from m3_avm_b200 import matvec_quant as MQ
     from m3_avm_b200 import model
 
@@ -234,7 +235,8 @@ def decode_leg(args, dev, world: int = 1) -> dict:
     bytes_tok = shape.weight_bytes_per_token()
     peaks, kind = measured_peaks()
     peak = float(peaks["hbm_gbs"])
-    nccl_per_token = {"nccl": 2 * shape.n_layers + 1, "peer-stores": 0, "head-only": 1, "single": 0}
+    nccl_per_token = {"nccl": 2 * shape.n_layers + 1, "peer-stores": 0, "head-only": 1, "head-only-peer": 0,
+                      "single": 0}
     out = {
         "workload": "llama-3.2-1b-shaped greedy decode, Q4_K_M mix (Q4_K attn/gate/up/embd, Q6_K down/head)",
         "prompt_tokens": DECODE_PROMPT, "generated_tokens": DECODE_GEN,

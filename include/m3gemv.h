@@ -278,7 +278,9 @@ M3G_API int m3g_decoder_truncate(m3g_decoder* dec, uint64_t n);
  * 2 peer stores from the GEMV epilogues over NVLink (chosen at creation when
  * every rank can map every other rank's buffers), 3 only the vocab head is
  * split (every rank keeps the layers; one NCCL all-reduce of the greedy key
- * per step; tuning key decode_shard_ffn = 0 at creation). */
+ * per step; tuning key decode_shard_ffn = 0 at creation), 4 only the head is
+ * split and the greedy keys merge by peer atomics over NVLink (no collective
+ * per step; chosen like 2). */
 M3G_API int m3g_decoder_exchange(const m3g_decoder* dec);
 /* Device logits of the last step and the engine's stream (a cudaStream_t). */
 M3G_API const float* m3g_decoder_logits_dev(const m3g_decoder* dec);

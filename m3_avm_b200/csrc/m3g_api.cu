@@ -609,6 +609,7 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
     mp.a.step = peers->step;
     mp.a.wait_cnt = peers->wait_cnt;
     mp.a.wait_mul = peers->wait_mul;
+    mp.a.key_by_step = peers->key_by_step;
   }
   if (grid_out) *grid_out = mp.grid;
   cudaError_t e = launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);

@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(256) k_embed(const uint8_t* __restrict__ w, in
 // atomicMax, and the step's bookkeeping; the key is cleared for the next step.
 __global__ void __launch_bounds__(32) k_pick_step(unsigned long long* key, int* pos, int* tokens, const int* nfixed,
                                                   int max_pos, int* last, int* step, const unsigned int* wait_cnt,
-                                                  unsigned int wait_mul, uint32_t* status) {
+                                                  unsigned int wait_mul, int key_by_step, uint32_t* status) {
   grid_dep_wait();
   grid_dep_launch();
   if (threadIdx.x != 0) return;
@@ -318,6 +318,7 @@ __global__ void __launch_bounds__(32) k_pick_step(unsigned long long* key, int* 
     const unsigned int target = static_cast<unsigned int>(*step + 1) * wait_mul;
     if (!wait_count_bounded(wait_cnt, target, 2000000000ull)) atomicOr(status, kStatusPeerTimeout);
   }
+  if (key_by_step) key += *step & 1;  // this step's slot (a rank one step ahead merges into the other)
   const unsigned long long k = *key;
   const int pick = k ? static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k)) : 0;  // 0: every logit NaN
   const int p = *pos, next = p + 1;
@@ -583,7 +584,8 @@ int enqueue_step(m3g_decoder* d) {
   const int h = static_cast<int>(d->cfg.hidden), F = static_cast<int>(d->cfg.ffn);
   const int L = static_cast<int>(d->cfg.n_layers), V = static_cast<int>(d->cfg.vocab);
   const int mp = static_cast<int>(d->cfg.max_pos);
-  const bool pp = d->world > 1 && d->p2p;
+  const bool pp = d->world > 1 && d->p2p;  // greedy keys merge by peer atomics
+  const bool pp_ffn = pp && d->shard_ffn;   // FFN rows exchanged by peer stores too
   // Exchange slots: 2l = silu(g)*u of layer l, 2l+1 = hidden after layer l, 2L = greedy key.
   auto exchange = [&](int slot, size_t region_off, size_t elem_off, bool rows) {
     m3g::PeerIO io;
@@ -616,7 +618,7 @@ int enqueue_step(m3g_decoder* d) {
     // q|k|v reads hidden, which holds every rank's rows of the previous layer
     m3g::PeerIO wq;
     const m3g::PeerIO* pq = nullptr;
-    if (pp && l > 0) {
+    if (pp_ffn && l > 0) {
       wait_on(wq, 2 * (l - 1) + 1);
       pq = &wq;
     }
@@ -654,7 +656,7 @@ int enqueue_step(m3g_decoder* d) {
                                        m3g::kAttnSplit, a));
     }
     if (int rc = gemv(d, part(T[kO]), d->att, nullptr, nullptr, d->hidden, m3g::kXPlain, d->hidden)) return rc;
-    if (pp) {  // this rank's rows, stored into every rank's buffers by the GEMV epilogues
+    if (pp_ffn) {  // this rank's rows, stored into every rank's buffers by the GEMV epilogues
       float* hslot = d->gub + static_cast<size_t>(d->rank) * d->Fr;
       const m3g::PeerIO gio = exchange(2 * l, d->off_gub, static_cast<size_t>(d->rank) * d->Fr, true);
       const Gemv& gu = d->gu[l];
@@ -699,7 +701,10 @@ int enqueue_step(m3g_decoder* d) {
     hio = exchange(2 * L, 0, 0, false);
     for (int p = 0; p < d->world; ++p)
       if (p != d->rank) hio.peer_key[p] = peer_at<unsigned long long>(d, p, d->off_key);
-    wait_on(hio, 2 * (L - 1) + 1);
+    hio.key_by_step = 1;
+    // with the FFN split the head's input holds every rank's rows of the last
+    // layer; with only the head split every rank computed all of it itself
+    if (pp_ffn) wait_on(hio, 2 * (L - 1) + 1);
     ph = &hio;
   }
   if (H.out > 0) {  // the last rank of a small vocabulary may hold no rows (NCCL path only)
@@ -715,7 +720,7 @@ int enqueue_step(m3g_decoder* d) {
   const unsigned int* pick_wait = pp ? d->cnt + 2 * L : nullptr;
   DEC_CUDA(m3g::launch_pdl(m3g::k_pick_step, dim3(1), dim3(32), 0, d->st, d->key, d->dpos, d->tokens,
                            static_cast<const int*>(d->nfixed), mp, d->last, d->dstep, pick_wait,
-                           static_cast<unsigned int>(d->world), d->status));
+                           static_cast<unsigned int>(d->world), pp ? 1 : 0, d->status));
   return M3G_OK;
 }
 
@@ -779,9 +784,12 @@ int check_status(m3g_decoder* d) {
 int setup_peers(m3g_decoder* d) {
   d->p2p = false;
   d->peer_base[d->rank] = d->xregion;
-  // peer stores keep the ranks in step through the per-layer exchanges; with
-  // only the head split, the greedy key is merged by an NCCL all-reduce
-  if (d->world < 2 || d->world > m3g::kMaxPeers || !m3g::decode_p2p_enabled() || !d->shard_ffn) return M3G_OK;
+  // With the FFN split, peer stores carry the rows and keep the ranks in step
+  // through the per-layer exchanges.  With only the head split, the ranks
+  // merge their greedy keys by peer atomics and may drift one step apart, so
+  // the key has one slot per step parity (a rank one step ahead can only have
+  // reached the next step's head: its pick waited for this rank's head).
+  if (d->world < 2 || d->world > m3g::kMaxPeers || !m3g::decode_p2p_enabled()) return M3G_OK;
   if (static_cast<long long>(d->cfg.vocab) - static_cast<long long>(d->world - 1) * d->Vr < 1) return M3G_OK;
   constexpr int kRec = 72;  // 64-byte handle + ok flag
   uint8_t rec[kRec] = {};
@@ -1106,7 +1114,10 @@ M3G_API int m3g_decoder_truncate(m3g_decoder* d, uint64_t n) {
   DEC_CUDA(cudaStreamSynchronize(d->st));
   const int p = static_cast<int>(n);
   DEC_CUDA(cudaMemcpy(d->dpos, &p, 4, cudaMemcpyHostToDevice));
-  DEC_CUDA(cudaMemset(d->key, 0, 16));
+  // Every step's pick leaves its key slot zero.  With peer merges a rank that
+  // truncated first may already have merged its next step's key here, so the
+  // slots are left alone then.
+  if (!d->p2p) DEC_CUDA(cudaMemset(d->key, 0, 16));
   d->pos = p;
   d->pending = false;
   return M3G_OK;
@@ -1116,7 +1127,7 @@ M3G_API const float* m3g_decoder_logits_dev(const m3g_decoder* d) { return d ? d
 
 M3G_API int m3g_decoder_exchange(const m3g_decoder* d) {
   if (!d) return -1;
-  return d->world == 1 ? 0 : (!d->shard_ffn ? 3 : (d->p2p ? 2 : 1));
+  return d->world == 1 ? 0 : (!d->shard_ffn ? (d->p2p ? 4 : 3) : (d->p2p ? 2 : 1));
 }
 
 M3G_API void* m3g_decoder_stream(const m3g_decoder* d) { return d ? static_cast<void*>(d->st) : nullptr; }

@@ -97,6 +97,10 @@ struct MmaArgs {
   const int* step;
   const unsigned int* wait_cnt;
   unsigned int wait_mul;
+  // 1: the greedy key of step *step is argmax_key[*step & 1] (and the same
+  // slot of every peer_key), so that a rank one step ahead merges into the
+  // other slot while this rank still reads the last one.
+  int key_by_step;
 };
 
 // Peer-exchange form of a decode GEMV (all pointers device-side; see MmaArgs).
@@ -109,6 +113,7 @@ struct PeerIO {
   const int* step = nullptr;
   const unsigned int* wait_cnt = nullptr;
   unsigned int wait_mul = 0;
+  int key_by_step = 0;
 };
 
 enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };

@@ -410,15 +410,19 @@ __device__ __forceinline__ void quantize_sb(const float (&v)[8], int sb, int lan
 // One CTA's arrival in a peer exchange (after its stores are fenced): the
 // CTA completing this step's count pushes the local greedy key to the peers
 // and signals each peer once.
+// Slot of the greedy key this step uses (see MmaArgs::key_by_step).
+__device__ __forceinline__ int key_slot(const MmaArgs& a) { return a.key_by_step ? (*a.step & 1) : 0; }
+
 __device__ __forceinline__ void peer_arrive(const MmaArgs& a) {
   const unsigned int target = static_cast<unsigned int>(*a.step + 1) * gridDim.x;
   const unsigned int prev = atomicAdd(a.done_cnt, 1u);
   if (prev + 1u != target) return;
   __threadfence_system();
   if (a.argmax_key) {
-    const unsigned long long k = atomicAdd(a.argmax_key, 0ull);
+    const int ks = key_slot(a);
+    const unsigned long long k = atomicAdd(a.argmax_key + ks, 0ull);
     for (int p = 0; p < a.npeer; ++p)
-      if (a.peer_key[p] && k) atomicMax_system(a.peer_key[p], k);
+      if (a.peer_key[p] && k) atomicMax_system(a.peer_key[p] + ks, k);
     __threadfence_system();
   }
   for (int p = 0; p < a.npeer; ++p) atomicAdd_system(a.peer_cnt[p], 1u);
@@ -569,7 +573,7 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
       if (a.argmax_key) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) best_key = max(best_key, __shfl_xor_sync(0xFFFFFFFFu, best_key, o));
-        if (lane == 0 && best_key) atomicMax(a.argmax_key, best_key);
+        if (lane == 0 && best_key) atomicMax(a.argmax_key + key_slot(a), best_key);
       }
       if (a.npeer) {  // this CTA's rows are in every peer's memory: count it
         __threadfence_system();

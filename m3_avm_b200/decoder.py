@@ -132,8 +132,9 @@ class GpuDecoder:
 
     @property
     def exchange(self) -> str:
-        """'single', 'nccl' or 'peer-stores' (how a sharded engine moves rows)."""
-        return {0: "single", 1: "nccl", 2: "peer-stores", 3: "head-only"}.get(
+        """'single', 'nccl', 'peer-stores', 'head-only' (NCCL key all-reduce) or
+        'head-only-peer' (peer key merge): how a sharded engine moves rows."""
+        return {0: "single", 1: "nccl", 2: "peer-stores", 3: "head-only", 4: "head-only-peer"}.get(
             int(_lib.load().m3g_decoder_exchange(self._h)), "?")
 
     @property

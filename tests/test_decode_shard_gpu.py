@@ -4,7 +4,9 @@ Each rank keeps its rows of ffn_gate/up/down and the vocab head (or only of
 the head, every rank keeping the layers); every row is computed exactly as on
 one GPU, so the sharded steps must reproduce the single-GPU logits and greedy
 tokens bit for bit -- with the rows exchanged by peer stores from the GEMV
-epilogues, with NCCL all-gathers, and with the head split alone.  Also: a rank that never
+epilogues, with NCCL all-gathers, and with the head split alone (greedy keys
+merged by an NCCL all-reduce, or by peer atomics into per-step-parity slots
+with no collective per step, across a cache truncation).  Also: a rank that never
 joins makes creation give up with M3G_ETIMEOUT (host-side failure detection,
 nothing waits on the GPU).
 """
@@ -36,8 +38,9 @@ def _run(shape, rank, world, uid, p2p=1, shard_ffn=1):
     logits = [d.forward_one(t) for t in PROMPT]
     d.clear_kv_cache()
     toks = d.generate(PROMPT, N_GEN)
+    exchange = d.exchange
     d.close()
-    return [lg.tobytes() for lg in logits], toks.tobytes()
+    return [lg.tobytes() for lg in logits], toks.tobytes(), exchange
 
 
 def _rank(rank, world, uid, p2p, shard_ffn, q):
@@ -51,8 +54,10 @@ def _rank(rank, world, uid, p2p, shard_ffn, q):
         q.put((rank, repr(e)))
 
 
-@pytest.mark.parametrize("p2p,shard_ffn", [(1, 1), (0, 1), (1, 0)], ids=["peer-stores", "nccl", "head-only"])
-def test_sharded_decode_matches_single_gpu_bitwise(p2p, shard_ffn):
+@pytest.mark.parametrize("p2p,shard_ffn,exchange", [(1, 1, "peer-stores"), (0, 1, "nccl"), (0, 0, "head-only"),
+                                                    (1, 0, "head-only-peer")],
+                         ids=["peer-stores", "nccl", "head-only", "head-only-peer"])
+def test_sharded_decode_matches_single_gpu_bitwise(p2p, shard_ffn, exchange):
     import multiprocessing as mp
 
     import torch
@@ -74,9 +79,11 @@ def test_sharded_decode_matches_single_gpu_bitwise(p2p, shard_ffn):
         assert p.exitcode == 0
     for r in range(world):
         assert not isinstance(res[r], str), res[r]
-    want_logits, want_toks = _run(SHAPE, 0, 1, None)
+    want_logits, want_toks, single = _run(SHAPE, 0, 1, None)
+    assert single == "single"
     for r in range(world):
-        got_logits, got_toks = res[r]
+        got_logits, got_toks, got_exchange = res[r]
+        assert got_exchange == exchange
         assert got_toks == want_toks
         for a, b in zip(got_logits, want_logits):
             assert a == b
