@@ -457,7 +457,8 @@ int gemv_batch_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, co
       pp.a.cols = static_cast<int>(cols);
       pp.a.ldy = static_cast<int>(out_dim);
       cudaError_t e = m3g::launch_umma_q4k(pp.a, x + p0 * in_dim, in_dim, pp.nb,
-                                           static_cast<int>(g_tune.umma_chains), pp.grid, pp.smem, st);
+                                           static_cast<int>(g_tune.umma_chains), pp.grid, pp.smem, st,
+                                           g_tune.pdl != 0);
       if (e != cudaSuccess) rc = cuda_fail(e, "tcgen05 batched GEMV launch");
       else g_launches.fetch_add(3, std::memory_order_relaxed);
     }

@@ -170,8 +170,10 @@ struct UmmaArgs {
   int NSB, cols, ldy, tiles, NSW, NSX;
   int off_x, off_am, off_bar;
 };
+// pdl: the GEMM kernel may start while the X prep runs (programmatic
+// dependent launch); it waits for the prep before reading X, scales, counters.
 cudaError_t launch_umma_q4k(const UmmaArgs& a, const float* x, long long in_dim, int nb, int chains, int grid,
-                            size_t smem, cudaStream_t st);
+                            size_t smem, cudaStream_t st, bool pdl);
 int umma_xtile(int nb);
 
 int mma_sb_bytes(int fmt);

@@ -211,6 +211,10 @@ __global__ void __launch_bounds__(256) k_umma_xprep(const float* __restrict__ x,
   float* gsum = xsm + NB * 257;
   float* sinv = gsum + NB * 8;
   const int s = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The GEMM kernel that follows may start now: it streams and decodes the
+  // weights, and waits for this grid before it touches X, the scales or the
+  // counters.
+  grid_dep_launch();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tiles; i += gridDim.x * blockDim.x) cnt[i] = 0u;
   for (int i = threadIdx.x; i < NB * 256; i += blockDim.x) {
     const int n = i >> 8, e = i & 255;
@@ -438,6 +442,7 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
     }
   } else if (warp < kProducer) {
     // ------------------------------------------------------------ readout / epilogue
+    grid_dep_wait();  // the column scales and the tile counters come from the X prep
     const int q = warp & 3, cb = kRd == 4 ? 0 : ((warp - kDec) >> 2) * RC;  // lane quarter, first column
     const int r = 32 * q + lane;
     const int rt = tid - kDec * 32;  // index within the readout warps
@@ -533,35 +538,56 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
   } else if (warp == kProducer) {
     // ------------------------------------------------------------ producer
     const uint64_t wpol = l2_evict_first_policy(), xpol = l2_evict_last_policy();
-    int issued = 0;
+    int wiss = 0, xiss = 0;  // weight and X stages issued
     if (lane == 0) {
       long long tile = it0 / a.NSB;
       int s = static_cast<int>(it0 - tile * a.NSB), ws = 0, wph = 0, xs = 0, xph = 0;
+      // The X prep never writes the weights: the first weight stages (all
+      // free at the start) stream while it finishes; the X tiles wait for it.
+      const int npre = min(K, a.NSW);
+      {
+        long long t2 = tile;
+        int s2 = s;
+        for (; wiss < npre; ++wiss) {
+          mbar_arrive_expect_tx(&wfull[wiss], static_cast<uint32_t>(kStageW));
+          tma_load_2d(smem + static_cast<size_t>(wiss) * kStageW, &wmap, s2 * (kSBBytes / 4),
+                      static_cast<int>(t2 * kTileRows), &wfull[wiss], wpol);
+          if (++s2 == a.NSB) s2 = 0, ++t2;
+        }
+      }
+      grid_dep_wait();
       for (int k = 0; k < K; ++k) {
         if (*abort_flag) break;
-        // weight stage free (decoders), X stage free (the MMAs of super-block k - NSX)
-        if (!mbar_wait_bounded(&wempty[ws], wph ^ 1, kUmmaTimeoutNs, abort_flag) ||
-            (k >= a.NSX && !wait_sb(k - a.NSX))) {
+        if (k >= npre) {  // weight stage free (decoders)
+          if (!mbar_wait_bounded(&wempty[ws], wph ^ 1, kUmmaTimeoutNs, abort_flag)) {
+            raise_timeout(abort_flag, a.status);
+            break;
+          }
+          mbar_arrive_expect_tx(&wfull[ws], static_cast<uint32_t>(kStageW));
+          tma_load_2d(smem + static_cast<size_t>(ws) * kStageW, &wmap, s * (kSBBytes / 4),
+                      static_cast<int>(tile * kTileRows), &wfull[ws], wpol);
+          wiss = k + 1;
+        }
+        // X stage free (the MMAs of super-block k - NSX)
+        if (k >= a.NSX && !wait_sb(k - a.NSX)) {
           raise_timeout(abort_flag, a.status);
           break;
         }
-        mbar_arrive_expect_tx(&wfull[ws], static_cast<uint32_t>(kStageW));
-        tma_load_2d(smem + static_cast<size_t>(ws) * kStageW, &wmap, s * (kSBBytes / 4),
-                    static_cast<int>(tile * kTileRows), &wfull[ws], wpol);
         mbar_arrive_expect_tx(&xfull[xs], XS);
         bulk_g2s(smem + a.off_x + static_cast<size_t>(xs) * XS, a.xt + static_cast<size_t>(s) * XS, XS, &xfull[xs],
                  xpol);
-        issued = k + 1;
+        xiss = k + 1;
         if (++ws == a.NSW) ws = 0, wph ^= 1;
         if (++xs == a.NSX) xs = 0, xph ^= 1;
         if (++s == a.NSB) s = 0, ++tile;
       }
     }
-    issued = __shfl_sync(0xFFFFFFFFu, issued, 0);
+    wiss = __shfl_sync(0xFFFFFFFFu, wiss, 0);
+    xiss = __shfl_sync(0xFFFFFFFFu, xiss, 0);
     // every copy this warp issued lands before the CTA can exit
-    for (int k = max(0, issued - a.NSW); k < issued; ++k)
+    for (int k = max(0, wiss - a.NSW); k < wiss; ++k)
       mbar_wait_bounded(&wfull[k % a.NSW], (k / a.NSW) & 1, kUmmaTimeoutNs, nullptr);
-    for (int k = max(0, issued - a.NSX); k < issued; ++k)
+    for (int k = max(0, xiss - a.NSX); k < xiss; ++k)
       mbar_wait_bounded(&xfull[k % a.NSX], (k / a.NSX) & 1, kUmmaTimeoutNs, nullptr);
   } else {
     // ------------------------------------------------------------ MMA issuers
@@ -632,41 +658,53 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }  // namespace
 
 template <int NB, int C>
-cudaError_t launch_q4k(const UmmaArgs& a, int grid, size_t smem, const CUtensorMap& wmap, cudaStream_t st) {
+cudaError_t launch_q4k(const UmmaArgs& a, int grid, size_t smem, const CUtensorMap& wmap, cudaStream_t st,
+                      bool pdl) {
   cudaError_t e = set_smem<k_umma_q4k<NB, C>>(smem);
   if (e != cudaSuccess) return e;
-  k_umma_q4k<NB, C><<<grid, umma_threads(NB, C), smem, st>>>(a, wmap);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the kernel may start while the X prep
+  // before it runs (see k_umma_xprep / the producer and readout waits).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(umma_threads(NB, C)));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_umma_q4k<NB, C>, a, wmap);
 }
 
 // Largest chain count that fits TMEM for NB columns, capped by the request.
 template <int NB>
 cudaError_t launch_nb(const UmmaArgs& a, const float* x, long long in_dim, int chains, int grid, size_t smem,
-                      int xprep_smem, const CUtensorMap& wmap, cudaStream_t st) {
+                      int xprep_smem, const CUtensorMap& wmap, cudaStream_t st, bool pdl) {
   cudaError_t e = set_smem<k_umma_xprep<NB>>(xprep_smem);
   if (e != cudaSuccess) return e;
   k_umma_xprep<NB><<<a.NSB, 256, xprep_smem, st>>>(x, a.cols, in_dim, const_cast<float*>(a.sig),
                                                     const_cast<uint8_t*>(a.xt), a.cnt, a.tiles);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if constexpr (NB == 8) {
-    if (chains >= 3) return launch_q4k<8, 3>(a, grid, smem, wmap, st);
-    if (chains >= 2) return launch_q4k<8, 2>(a, grid, smem, wmap, st);
-    return launch_q4k<8, 1>(a, grid, smem, wmap, st);
+    if (chains >= 3) return launch_q4k<8, 3>(a, grid, smem, wmap, st, pdl);
+    if (chains >= 2) return launch_q4k<8, 2>(a, grid, smem, wmap, st, pdl);
+    return launch_q4k<8, 1>(a, grid, smem, wmap, st, pdl);
   } else if constexpr (NB == 16) {
-    if (chains >= 3) return launch_q4k<16, 3>(a, grid, smem, wmap, st);
-    if (chains >= 2) return launch_q4k<16, 2>(a, grid, smem, wmap, st);
-    return launch_q4k<16, 1>(a, grid, smem, wmap, st);
+    if (chains >= 3) return launch_q4k<16, 3>(a, grid, smem, wmap, st, pdl);
+    if (chains >= 2) return launch_q4k<16, 2>(a, grid, smem, wmap, st, pdl);
+    return launch_q4k<16, 1>(a, grid, smem, wmap, st, pdl);
   } else if constexpr (NB == 32) {
-    if (chains >= 3) return launch_q4k<32, 3>(a, grid, smem, wmap, st);
-    if (chains >= 2) return launch_q4k<32, 2>(a, grid, smem, wmap, st);
-    return launch_q4k<32, 1>(a, grid, smem, wmap, st);
+    if (chains >= 3) return launch_q4k<32, 3>(a, grid, smem, wmap, st, pdl);
+    if (chains >= 2) return launch_q4k<32, 2>(a, grid, smem, wmap, st, pdl);
+    return launch_q4k<32, 1>(a, grid, smem, wmap, st, pdl);
   } else {
-    return launch_q4k<64, 1>(a, grid, smem, wmap, st);
+    return launch_q4k<64, 1>(a, grid, smem, wmap, st, pdl);
   }
 }
 
 cudaError_t launch_umma_q4k(const UmmaArgs& a, const float* x, long long in_dim, int nb, int chains, int grid,
-                            size_t smem, cudaStream_t st) {
+                            size_t smem, cudaStream_t st, bool pdl) {
   // The weight matrix as rows x (RB / 4) words; one box = one super-block of 128 rows.
   auto encode = tensor_map_encoder();
   if (!encode) return cudaErrorNotSupported;
@@ -682,10 +720,10 @@ cudaError_t launch_umma_q4k(const UmmaArgs& a, const float* x, long long in_dim,
   const int xprep_smem = (nb * 257 + nb * 8 + nb) * 4;
   cudaError_t e = cudaSuccess;
   switch (nb) {
-    case 8: e = launch_nb<8>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
-    case 16: e = launch_nb<16>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
-    case 32: e = launch_nb<32>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
-    case 64: e = launch_nb<64>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st); break;
+    case 8: e = launch_nb<8>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st, pdl); break;
+    case 16: e = launch_nb<16>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st, pdl); break;
+    case 32: e = launch_nb<32>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st, pdl); break;
+    case 64: e = launch_nb<64>(a, x, in_dim, chains, grid, smem, xprep_smem, wmap, st, pdl); break;
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess) return e;
