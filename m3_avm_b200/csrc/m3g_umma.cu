@@ -153,9 +153,10 @@ __device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
-// Two small integers (< 1024) as an fp16 pair: (1024 + v) - 1024, exact.
-__device__ __forceinline__ uint32_t int_pair_f16(uint32_t lo, uint32_t hi) {
-  return hfma2(0x64006400u | lo | (hi << 16), 0x3C003C00u, 0xE400E400u);
+// The bytes that selector nibbles 0 and 2 pick from the 8 bytes {hi:lo}, as
+// an fp16 pair of small integers: (1024 + v) - 1024, exact.
+__device__ __forceinline__ uint32_t byte_pair_f16(uint32_t lo, uint32_t hi, uint32_t sel) {
+  return hfma2(0x64006400u | (__byte_perm(lo, hi, sel) & 0x00FF00FFu), 0x3C003C00u, 0xE400E400u);
 }
 
 __device__ __forceinline__ uint64_t l2_evict_last_policy() {
@@ -383,17 +384,18 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
       const uint32_t sc_lo = hd.y & 0x3F3F3F3Fu, m_lo = hd.z & 0x3F3F3F3Fu;
       const uint32_t sc_hi = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
       const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
-      auto byte_of = [&](uint32_t lo, uint32_t hi, int g) { return ((g < 4 ? lo : hi) >> (8 * (g & 3))) & 0xFFu; };
+      // byte_perm selector of group g into result bytes 0 and 2
+      auto sel2 = [](int ga, int gb) { return static_cast<uint32_t>(ga) | (static_cast<uint32_t>(gb) << 8); };
       // low nibbles enter as 1024 + q, high nibbles in place as 1024 + 16 q:
       // q*sc = (1024 + q)*sc - 1024*sc = (1024 + 16q)*(sc/16) - 64*sc, exact
       constexpr int NG = kVecs / 2 > 0 ? kVecs / 2 : 1;  // vector pairs = group pairs
       uint32_t SL[NG], NL[NG], SH[NG], NH[NG];
 #pragma unroll
       for (int j = 0; j < NG; ++j) {
-        const uint32_t sl = byte_of(sc_lo, sc_hi, g0 + 2 * j), sh = byte_of(sc_lo, sc_hi, g0 + 2 * j + 1);
-        SL[j] = int_pair_f16(sl, sl);
+        const int ga = g0 + 2 * j, gb = ga + 1;
+        SL[j] = byte_pair_f16(sc_lo, sc_hi, sel2(ga, ga));
         NL[j] = hfma2(SL[j], 0xE400E400u, 0x80008000u);  // -1024 * sc
-        const uint32_t S = int_pair_f16(sh, sh);
+        const uint32_t S = byte_pair_f16(sc_lo, sc_hi, sel2(gb, gb));
         SH[j] = hfma2(S, 0x2C002C00u, 0x80008000u);      // sc / 16
         NH[j] = hfma2(S, 0xD400D400u, 0x80008000u);      // -64 * sc
       }
@@ -416,14 +418,12 @@ __global__ void __launch_bounds__(umma_threads(NB, C), 1)
         // 32 * m (<= 2016, exact in fp16) against the group sums / 32
         uint8_t* dst = am + buf * kAmBytes + (r >> 3) * 256 + (r & 7) * 16 + 2 * g0;
         if constexpr (kVecs == 4) {
-          const uint32_t m01 = hfma2(int_pair_f16(byte_of(m_lo, m_hi, g0), byte_of(m_lo, m_hi, g0 + 1)),
-                                     0x50005000u, 0x80008000u);
-          const uint32_t m23 = hfma2(int_pair_f16(byte_of(m_lo, m_hi, g0 + 2), byte_of(m_lo, m_hi, g0 + 3)),
-                                     0x50005000u, 0x80008000u);
+          const uint32_t m01 = hfma2(byte_pair_f16(m_lo, m_hi, sel2(g0, g0 + 1)), 0x50005000u, 0x80008000u);
+          const uint32_t m23 = hfma2(byte_pair_f16(m_lo, m_hi, sel2(g0 + 2, g0 + 3)), 0x50005000u, 0x80008000u);
           *reinterpret_cast<uint2*>(dst) = make_uint2(m01, m23);
         } else {
-          *reinterpret_cast<uint32_t*>(dst) = hfma2(
-              int_pair_f16(byte_of(m_lo, m_hi, g0), byte_of(m_lo, m_hi, g0 + 1)), 0x50005000u, 0x80008000u);
+          *reinterpret_cast<uint32_t*>(dst) =
+              hfma2(byte_pair_f16(m_lo, m_hi, sel2(g0, g0 + 1)), 0x50005000u, 0x80008000u);
         }
       }
       if (part == 0) {
