@@ -215,6 +215,22 @@ M3G_API int m3g_matvec_fused_dev(const float* x, const float* x2, const float* g
                                  int swiglu, const uint8_t* raw, uint64_t raw_len, uint32_t dtype, uint64_t in_dim,
                                  uint64_t out_dim, float* y, void* stream);
 
+/* The same GEMV with its input gated on a device counter, for an x that
+ * another stream, process or GPU produces and then signals by incrementing
+ * *ready_cnt (device memory, 4-byte aligned).  The weight stream starts at
+ * once; the x preparation waits until *ready_cnt >= ready_target (wrap-safe
+ * comparison) before reading x -- the wait a sharded decode step makes for the
+ * rows other GPUs store into it (src/inference.rs:1083-1103 are the steps it
+ * gates).  The wait is bounded by the tuning key "peer_wait_us" (default
+ * 2 s): when it runs out the kernel sets bit 8 (kStatusPeerTimeout) of the
+ * device status word (m3g_device_status), computes with x as it is and
+ * returns; the context stays usable.  No swiglu form.  M3G_EINVAL where
+ * m3g_matvec_fused_dev gives it. */
+M3G_API int m3g_matvec_fused_wait_dev(const float* x, const float* x2, const float* gamma, const float* res,
+                                      int xmode, const uint8_t* raw, uint64_t raw_len, uint32_t dtype,
+                                      uint64_t in_dim, uint64_t out_dim, float* y, const uint32_t* ready_cnt,
+                                      uint32_t ready_target, void* stream);
+
 /* ---------------------------------------------------------------- device-resident greedy decode
  *
  * RealInference::forward_one (src/inference.rs:953-1152) for a Llama-style
@@ -318,9 +334,15 @@ M3G_API int m3g_vm_ffn_dev(const float* x, uint64_t M, uint64_t D, const uint8_t
  * sample_with_params with top_k = 1 -- computed by the tensor-core GEMV with
  * its argmax epilogue.  Allocates no device memory: the logits and the
  * reduction key live in a static device array of this library, so out_dim is
- * at most 262144 (M3G_EINVAL beyond).  The first call on a device (with
- * that device current) sets up that array's address; make it before any
- * stream capture begins.  One call at a time per device: overlapping calls
+ * at most 262144 (M3G_EINVAL beyond).  It runs only on the tensor-core plan:
+ * in_dim % 256 == 0, rows of a whole number of 16 bytes (Q4_K, Q8_0, Q4_0
+ * rows always are; Q6_K needs in_dim % 2048 == 0), raw and x 16-byte
+ * aligned; M3G_EINVAL ("no tensor-core plan") otherwise.  The first call on a
+ * device (with that device current) sets up that array's address; make it
+ * before any stream capture begins.  A call that finds another context
+ * current than at set-up (after cudaDeviceReset) repeats the set-up, so make
+ * the first call after a reset outside a capture too.  One call at a time per
+ * device: overlapping calls
  * on different streams share the array and race.  *token = 0xFFFFFFFF when a
  * bounded wait inside the GEMV gave up.  Enqueues on `stream` (NULL = the
  * legacy default stream) and returns without waiting. */
@@ -330,17 +352,21 @@ M3G_API int m3g_matvec_greedy_noalloc(const float* x, const uint8_t* raw, uint64
 /* ---------------------------------------------------------------- diagnostics */
 
 /* Error word the kernels of `device` set when a bounded wait gives up
- * (bit 0: a staged-copy wait timed out).  clear != 0 resets it.  Synchronises
- * the device. */
+ * (bit 0: a staged-copy wait timed out; bit 3, value 8: a wait for a counter
+ * bumped by another GPU or producer ran out, see "peer_wait_us").  clear != 0
+ * resets it.  Synchronises the device. */
 M3G_API int m3g_device_status(int device, uint32_t* out, int clear);
 
 /* Number of kernel launches this library has enqueued in this process. */
 M3G_API uint64_t m3g_launch_count(void);
 
 /* Launch-shape knobs of the streaming GEMV ("stage_bytes", "ctas_per_sm",
- * "max_stages") and "force_generic" (route every GEMV through the
- * row-straddling generic kernel).  Process-wide; M3G_ENONE for an unknown key
- * or out-of-range value.  No counterpart in the reference. */
+ * "max_stages"), "force_generic" (route every GEMV through the
+ * row-straddling generic kernel) and "peer_wait_us" (limit, in microseconds,
+ * of a kernel's wait for a counter bumped by another GPU or producer; default
+ * 2000000; read when a GEMV is enqueued or a decode step captured).
+ * Process-wide; M3G_ENONE for an unknown key or out-of-range value.  No
+ * counterpart in the reference. */
 M3G_API int m3g_set_tuning(const char* key, int64_t value);
 
 #ifdef __cplusplus

@@ -73,6 +73,8 @@ SIGNATURES: dict[str, tuple] = {
     "m3g_shard_destroy": (None, [_vp]),
     "m3g_matvec_fused_dev": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _u64, _u32, _u64,
                                             _u64, _vp, _vp]),
+    "m3g_matvec_fused_wait_dev": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, _vp, _u64, _u32, _u64, _u64,
+                                                 _vp, _vp, _u32, _vp]),
     "m3g_decoder_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(DecoderConfig), ctypes.POINTER(_vp)]),
     "m3g_decoder_create_sharded": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(DecoderConfig), ctypes.c_int,
                                                   ctypes.c_int, _vp, ctypes.c_double, ctypes.POINTER(_vp)]),

@@ -97,6 +97,7 @@ struct Tuning {
   int64_t umma = 1;               // batched Q4_K on tcgen05 (k_umma_q4k), up to 64 columns per pass
   int64_t umma_chains = 8;        // independent accumulators per super-block (capped by TMEM)
   int64_t offload_graph = 1;      // host-buffer offload calls replay one CUDA graph (copy in, GEMV, copy out)
+  int64_t peer_wait_us = 2000000; // limit of a kernel's wait for a counter bumped by other GPUs
 };
 Tuning g_tune;
 
@@ -293,6 +294,7 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   p.a.SEG = static_cast<int>(seg);
   p.a.NS = static_cast<int>(NS);
   p.a.PRE = static_cast<int>(std::max<int64_t>(0, g_tune.mma_pre));
+  p.a.peer_wait_ns = static_cast<unsigned long long>(g_tune.peer_wait_us) * 1000ull;
   p.tps = tps;
   p.wk = wk;
   const long long ctas = static_cast<long long>(ds.sms) * mctas;
@@ -649,6 +651,7 @@ int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const flo
 }
 
 bool decode_p2p_enabled() { return g_tune.decode_p2p != 0; }
+unsigned long long peer_wait_ns() { return static_cast<unsigned long long>(g_tune.peer_wait_us) * 1000ull; }
 bool decode_shard_ffn_enabled() { return g_tune.decode_shard_ffn != 0; }
 
 int status_word(int device, uint32_t** out) {
@@ -704,6 +707,7 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "umma")) g_tune.umma = value != 0;
   else if (!strcmp(key, "offload_graph")) g_tune.offload_graph = value != 0;
   else if (!strcmp(key, "umma_chains") && value >= 1 && value <= 8) g_tune.umma_chains = value;
+  else if (!strcmp(key, "peer_wait_us") && value >= 1 && value <= 60000000) g_tune.peer_wait_us = value;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }
@@ -960,10 +964,15 @@ struct m3g_offload {
   uint64_t max_in = 0, max_out = 0;
   uint64_t cap_batch = 0;
   float* d_x = nullptr;
-  float* d_y = nullptr;
-  float* h_x = nullptr;  // pinned staging
-  float* h_y = nullptr;
-  uint32_t* h_status = nullptr;
+  // Host-buffer calls write y into d_out + 16 and report kernel status in the
+  // context's own word at d_out, so one copy brings both back to h_out.
+  uint8_t* d_out = nullptr;
+  float* d_y = nullptr;           // d_out + 16
+  uint32_t* d_status = nullptr;   // d_out
+  float* h_x = nullptr;           // pinned staging
+  uint8_t* h_out = nullptr;       // pinned: [status (16 bytes)][y]
+  float* h_y = nullptr;           // h_out + 16
+  uint32_t* h_status = nullptr;   // h_out
   uint64_t calls = 0;
   std::unordered_map<uint64_t, ResidentTensor> tensors;
   // Host-buffer calls: one captured graph per tensor (copy x in, GEMV, copy y
@@ -1000,12 +1009,12 @@ void drop_graphs(m3g_offload* c) {
 void free_io(m3g_offload* c) {
   drop_graphs(c);
   if (c->d_x) cudaFree(c->d_x);
-  if (c->d_y) cudaFree(c->d_y);
+  if (c->d_out) cudaFree(c->d_out);
   if (c->h_x) cudaFreeHost(c->h_x);
-  if (c->h_y) cudaFreeHost(c->h_y);
-  if (c->h_status) cudaFreeHost(c->h_status);
+  if (c->h_out) cudaFreeHost(c->h_out);
   c->d_x = c->d_y = c->h_x = c->h_y = nullptr;
-  c->h_status = nullptr;
+  c->d_out = c->h_out = nullptr;
+  c->d_status = c->h_status = nullptr;
   c->cap_batch = 0;
 }
 
@@ -1015,10 +1024,14 @@ int ensure_io(m3g_offload* c, uint64_t batch) {
   const size_t nx = static_cast<size_t>(std::max<uint64_t>(c->max_in, 16) * batch);
   const size_t ny = static_cast<size_t>(std::max<uint64_t>(c->max_out, 16) * batch);
   M3G_CUDA(cudaMalloc(&c->d_x, nx * sizeof(float)));
-  M3G_CUDA(cudaMalloc(&c->d_y, ny * sizeof(float)));
+  M3G_CUDA(cudaMalloc(&c->d_out, 16 + ny * sizeof(float)));
+  M3G_CUDA(cudaMemset(c->d_out, 0, 16));
   M3G_CUDA(cudaMallocHost(&c->h_x, nx * sizeof(float)));
-  M3G_CUDA(cudaMallocHost(&c->h_y, ny * sizeof(float)));
-  M3G_CUDA(cudaMallocHost(&c->h_status, 16));
+  M3G_CUDA(cudaMallocHost(&c->h_out, 16 + ny * sizeof(float)));
+  c->d_status = reinterpret_cast<uint32_t*>(c->d_out);
+  c->d_y = reinterpret_cast<float*>(c->d_out + 16);
+  c->h_status = reinterpret_cast<uint32_t*>(c->h_out);
+  c->h_y = reinterpret_cast<float*>(c->h_out + 16);
   c->cap_batch = batch;
   return M3G_OK;
 }
@@ -1156,12 +1169,20 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
   memcpy(c->h_x, x, bx);
   DevState* ds = nullptr;
   if (int rc = dev_state(c->device, &ds)) return rc;
-  // copy in, GEMV, copy out and the status word, on c->stream
+  // The kernels of this call report into the context's status word, which
+  // travels back in the same copy as y.
+  DevState dsc = *ds;
+  dsc.status = c->d_status;
+  FmtInfo f;
+  fmt_info(t.dtype, f);
+  // copy in, GEMV, one copy out of [status | y], on c->stream
   auto enqueue = [&]() -> int {
     M3G_CUDA(cudaMemcpyAsync(c->d_x, c->h_x, bx, cudaMemcpyHostToDevice, c->stream));
-    if (int rc = m3g_offload_matvec_dev(c, tidx, c->d_x, batch, c->d_y, c->stream)) return rc;
-    M3G_CUDA(cudaMemcpyAsync(c->h_y, c->d_y, by, cudaMemcpyDeviceToHost, c->stream));
-    M3G_CUDA(cudaMemcpyAsync(c->h_status, ds->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+    if (int rc = gemv_batch_launch(dsc, f, t.d_raw, c->d_x, c->d_y, static_cast<long long>(t.in_dim),
+                                   static_cast<long long>(t.out_dim), static_cast<long long>(batch), c->stream))
+      return rc;
+    ++c->calls;
+    M3G_CUDA(cudaMemcpyAsync(c->h_out, c->d_out, 16 + by, cudaMemcpyDeviceToHost, c->stream));
     return M3G_OK;
   };
   m3g_offload::HostGraph* hg = nullptr;
@@ -1200,9 +1221,10 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
   }
   M3G_CUDA(cudaStreamSynchronize(c->stream));
   memcpy(y, c->h_y, by);
-  if (*c->h_status & m3g::kStatusCopyTimeout) {
-    cudaMemset(ds->status, 0, sizeof(uint32_t));
-    return fail(M3G_ETIMEOUT, "a staged weight copy did not complete in time");
+  if (*c->h_status) {
+    const uint32_t bits = *c->h_status;
+    cudaMemset(c->d_status, 0, sizeof(uint32_t));
+    return fail(M3G_ETIMEOUT, "a bounded wait in the GEMV gave up (status 0x%x)", bits);
   }
   return M3G_OK;
 }

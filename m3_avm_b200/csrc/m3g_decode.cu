@@ -310,13 +310,14 @@ __global__ void __launch_bounds__(256) k_embed(const uint8_t* __restrict__ w, in
 // atomicMax, and the step's bookkeeping; the key is cleared for the next step.
 __global__ void __launch_bounds__(32) k_pick_step(unsigned long long* key, int* pos, int* tokens, const int* nfixed,
                                                   int max_pos, int* last, int* step, const unsigned int* wait_cnt,
-                                                  unsigned int wait_mul, int key_by_step, uint32_t* status) {
+                                                  unsigned int wait_mul, int key_by_step, uint32_t* status,
+                                                  unsigned long long wait_ns) {
   grid_dep_wait();
   grid_dep_launch();
   if (threadIdx.x != 0) return;
   if (wait_cnt) {  // sharded with peer stores: every rank's head CTAs have merged their keys
     const unsigned int target = static_cast<unsigned int>(*step + 1) * wait_mul;
-    if (!wait_count_bounded(wait_cnt, target, 2000000000ull)) atomicOr(status, kStatusPeerTimeout);
+    if (!wait_count_bounded(wait_cnt, target, wait_ns)) atomicOr(status, kStatusPeerTimeout);
   }
   if (key_by_step) key += *step & 1;  // this step's slot (a rank one step ahead merges into the other)
   const unsigned long long k = *key;
@@ -720,7 +721,7 @@ int enqueue_step(m3g_decoder* d) {
   const unsigned int* pick_wait = pp ? d->cnt + 2 * L : nullptr;
   DEC_CUDA(m3g::launch_pdl(m3g::k_pick_step, dim3(1), dim3(32), 0, d->st, d->key, d->dpos, d->tokens,
                            static_cast<const int*>(d->nfixed), mp, d->last, d->dstep, pick_wait,
-                           static_cast<unsigned int>(d->world), pp ? 1 : 0, d->status));
+                           static_cast<unsigned int>(d->world), pp ? 1 : 0, d->status, m3g::peer_wait_ns()));
   return M3G_OK;
 }
 
@@ -1183,6 +1184,26 @@ M3G_API int m3g_matvec_fused_dev(const float* x, const float* x2, const float* g
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;
   return m3g::gemv_fused(dev, dtype, raw, raw_len, x, x2, gamma, res, xmode, y, static_cast<long long>(in_dim),
                          static_cast<long long>(out_dim), st, false, nullptr, swiglu != 0);
+}
+
+
+// The fused GEMV of m3g_matvec_fused_dev whose input is gated on a device
+// counter: the kernel's weight stream starts at once, and its x preparation
+// waits (bounded) until *ready_cnt >= ready_target before reading x.
+M3G_API int m3g_matvec_fused_wait_dev(const float* x, const float* x2, const float* gamma, const float* res,
+                                      int xmode, const uint8_t* raw, uint64_t raw_len, uint32_t dtype,
+                                      uint64_t in_dim, uint64_t out_dim, float* y, const uint32_t* ready_cnt,
+                                      uint32_t ready_target, void* stream) {
+  if (!x || !raw || !y || !ready_cnt) return host_fail(M3G_EINVAL, "null argument");
+  if (reinterpret_cast<uintptr_t>(ready_cnt) % 4) return host_fail(M3G_EINVAL, "ready counter not 4-byte aligned");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return host_fail(M3G_ECUDA, "no CUDA device");
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;
+  m3g::PeerIO io;
+  io.wait_cnt = reinterpret_cast<const unsigned int*>(ready_cnt);
+  io.wait_mul = ready_target;
+  return m3g::gemv_fused(dev, dtype, raw, raw_len, x, x2, gamma, res, xmode, y, static_cast<long long>(in_dim),
+                         static_cast<long long>(out_dim), st, false, nullptr, false, 0, &io);
 }
 
 }  // extern "C"

@@ -88,7 +88,9 @@ struct MmaArgs {
   // the CTA that completes this step's count ((*step + 1) * gridDim.x) merges
   // the local greedy key into the non-null peer_key[p] and adds 1 to every
   // peer_cnt[p] (p < npeer, this rank included).  Before reading x, the
-  // consumers wait until *wait_cnt >= (*step + 1) * wait_mul.
+  // consumers wait until *wait_cnt >= (*step + 1) * wait_mul (>= wait_mul
+  // when step is null), for at most peer_wait_ns; a wait that runs out sets
+  // kStatusPeerTimeout and the kernel goes on with x as it is.
   float* peer_y[kMaxPeers];
   unsigned long long* peer_key[kMaxPeers];
   unsigned int* peer_cnt[kMaxPeers];
@@ -97,6 +99,7 @@ struct MmaArgs {
   const int* step;
   const unsigned int* wait_cnt;
   unsigned int wait_mul;
+  unsigned long long peer_wait_ns;
   // 1: the greedy key of step *step is argmax_key[*step & 1] (and the same
   // slot of every peer_key), so that a rank one step ahead merges into the
   // other slot while this rank still reads the last one.
@@ -133,6 +136,10 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
 int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const float* x, float* y, long long in_dim,
                    long long out_dim, cudaStream_t st, int sms, int smem_per_sm, int smem_optin, uint32_t* status,
                    unsigned long long* key);
+
+// Limit of a kernel's wait for a counter that other GPUs (or another
+// producer) bump: the tuning key peer_wait_us, 2 s by default.
+unsigned long long peer_wait_ns();
 
 // Whether a sharded decoder may exchange rows by peer stores (tuning knob).
 bool decode_p2p_enabled();

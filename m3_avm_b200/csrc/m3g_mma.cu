@@ -684,8 +684,8 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
       grid_dep_launch();
       if (a.wait_cnt) {  // x holds other GPUs' rows: wait until every rank's CTAs have stored theirs
         if (lane == 0) {
-          const unsigned int target = static_cast<unsigned int>(*a.step + 1) * a.wait_mul;
-          if (!wait_count_bounded(a.wait_cnt, target, kMmaTimeoutNs)) atomicOr(a.status, kStatusPeerTimeout);
+          const unsigned int target = a.step ? static_cast<unsigned int>(*a.step + 1) * a.wait_mul : a.wait_mul;
+          if (!wait_count_bounded(a.wait_cnt, target, a.peer_wait_ns)) atomicOr(a.status, kStatusPeerTimeout);
         }
         __syncwarp();
       }

@@ -12,13 +12,16 @@
 // Setup: the first call on a device (with that device current) looks up the
 // array's device address with cudaGetSymbolAddress and reads the SM count
 // and shared-memory limits; later calls reuse them.  Make that first call
-// before any stream capture begins.
+// before any stream capture begins.  The address belongs to the device's
+// current context: a call that finds another context current (after
+// cudaDeviceReset, say) repeats the set-up instead of using a stale address.
 //
 // Limits and sharing: at most kMaxRows output rows (the logits fit the
 // array); one call at a time per device -- calls on different streams that
 // overlap use the same array and race.  Calls on one stream are ordered.
 #include <mutex>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "../../include/m3gemv.h"
@@ -41,11 +44,33 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 struct DevSetup {
   unsigned char* scratch = nullptr;
+  CUcontext ctx = nullptr;  // context the address was looked up in
   int sms = 0, smem_per_sm = 0, smem_optin = 0;
 };
 constexpr int kMaxDev = 64;
 std::mutex g_mu;
 DevSetup g_setup[kMaxDev];
+
+// cuCtxGetCurrent through the runtime's driver entry point (no libcuda link).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(p);
+    return static_cast<CtxGetCurrentFn>(nullptr);
+  }();
+  return fn;
+}
+
+CUcontext current_context() {
+  CUcontext c = nullptr;
+  CtxGetCurrentFn fn = ctx_get_current();
+  if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
 
 int setup_current_device(DevSetup* out) {
   int dev = 0;
@@ -54,12 +79,16 @@ int setup_current_device(DevSetup* out) {
   if (dev < 0 || dev >= kMaxDev) return m3g::host_fail(M3G_EINVAL, "device %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_mu);
   DevSetup& s = g_setup[dev];
-  if (!s.scratch) {
+  // A context other than the one the address came from (the device was
+  // reset, or no context is current on this thread yet) repeats the look-up.
+  const bool by_ctx = ctx_get_current() != nullptr;
+  if (!s.scratch || (by_ctx && current_context() != s.ctx)) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
     DevSetup t;
     t.scratch = static_cast<unsigned char*>(p);
+    t.ctx = by_ctx ? current_context() : nullptr;
     if ((e = cudaDeviceGetAttribute(&t.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
         (e = cudaDeviceGetAttribute(&t.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev)) !=
             cudaSuccess ||

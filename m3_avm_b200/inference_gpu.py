@@ -49,12 +49,20 @@ class GpuOffload:
     def calls(self) -> int:
         return int(_lib.load().m3g_offload_calls(self._h))
 
-    def matvec(self, tidx: int, x, in_dim: int, out_dim: int):
-        """src/inference_gpu.rs:188-237: y as float32, or None."""
-        xa = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    def matvec(self, tidx: int, x, in_dim: int, out_dim: int, out=None):
+        """src/inference_gpu.rs:188-237: y as float32, or None.  `out` (a
+        C-contiguous float32 array of out_dim values) receives y instead of a
+        new array, so a caller's token loop allocates nothing per call."""
+        xa = x if (isinstance(x, np.ndarray) and x.dtype == np.float32 and x.flags.c_contiguous) else \
+            np.ascontiguousarray(x, dtype=np.float32)
         if xa.size != in_dim:
             return None
-        y = np.empty(out_dim, np.float32)
+        if out is None:
+            y = np.empty(out_dim, np.float32)
+        else:
+            if out.dtype != np.float32 or out.size != out_dim or not out.flags.c_contiguous:
+                raise ValueError("out must be a C-contiguous float32 array of out_dim values")
+            y = out
         rc = _lib.load().m3g_offload_matvec(self._h, tidx, xa.ctypes.data, in_dim, out_dim, y.ctypes.data)
         return y if rc == _lib.M3G_OK else None
 

@@ -126,6 +126,24 @@ def matvec_fused_dev(x, raw, dtype: int, in_dim: int, out_dim: int, xmode: int =
     return y
 
 
+def matvec_fused_wait_dev(x, raw, dtype: int, in_dim: int, out_dim: int, ready, target: int, xmode: int = X_PLAIN,
+                          x2=None, gamma=None, res=None, y=None, stream=None):
+    """m3g_matvec_fused_wait_dev over CUDA tensors: the fused GEMV whose x
+    preparation first waits (bounded by the tuning key peer_wait_us) until the
+    device counter `ready` (an int32/uint32 tensor) reaches `target`."""
+    import torch
+
+    if y is None:
+        y = torch.empty(out_dim, dtype=torch.float32, device=x.device)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+    ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+    rc = _lib.load().m3g_matvec_fused_wait_dev(x.data_ptr(), ptr(x2), ptr(gamma), ptr(res), xmode, raw.data_ptr(),
+                                               raw.numel(), dtype, in_dim, out_dim, y.data_ptr(), ready.data_ptr(),
+                                               int(target) & 0xFFFFFFFF, ctypes.c_void_p(st))
+    _lib.check(rc)
+    return y
+
+
 def matvec_greedy_noalloc(x, raw, dtype: int, in_dim: int, out_dim: int, token=None, stream=None):
     """Greedy pick of W x into a device uint32 (m3g_matvec_greedy_noalloc): the
     library allocates nothing for it.  Returns the int32-typed token tensor."""

@@ -1,7 +1,9 @@
 """m3g_matvec_greedy_noalloc: the greedy vocab head that allocates no device
-memory, checked against the existing entry points (the GEMV of
-m3g_matvec_quant_dev, then the first index of the maximum) on two calls in
-a row.  Collected last so it also runs after every other GPU test."""
+memory, checked on two calls in a row against the existing entry points (the
+GEMV of m3g_matvec_quant_dev, then the first index of the maximum) and
+against the oracle's logits (the pick must be a row whose oracle logit is
+within the GEMV tolerance of the largest).  Collected last so it also runs
+after every other GPU test."""
 import numpy as np
 import pytest
 
@@ -58,6 +60,11 @@ def test_noalloc_greedy_matches_existing_entry_twice(torch_cuda):
         assert torch.cuda.mem_get_info(dev)[0] == free_before  # nothing allocated by the call
         got = int(token.item())
         assert got == want or got in near, (got, want, sorted(near)[:5])
+        # the oracle's logits: the pick is the top row, or a row that the
+        # per-row tolerance cannot tell apart from it
+        ref = O.matvec_quant(xh, raw_h, DTYPE, IN_DIM, OUT_DIM).astype(np.float64)
+        rb = O.gemv_bound(raw_h, DTYPE, IN_DIM, OUT_DIM, xh)
+        assert ref[got] + rb[got] >= np.max(ref - rb), (got, int(np.argmax(ref)))
     assert torch.cuda.mem_get_info(dev)[0] <= free0 + 0  # no growth after setup either
 
 
