@@ -762,6 +762,7 @@ def gemv_leg(args, dev, rank: int, world: int, in_dim: int, out_dim: int, dtype:
     per_step_s = ms / 1e3 / K
     abytes = algorithmic_bytes(in_dim, out_dim, dtype)
     out = {"per_step_s": per_step_s, "ms": ms, "windows": t["windows"], "weight_copies": n,
+           "exchange": s.exchange if use_shard else "single",
            "weight_set_mb": round(n * bytes_local / 2**20, 1), "l2_mb": round(l2 / 2**20, 1),
            "bytes_local": bytes_local, "rows_local": rows_local, "abytes": abytes,
            "warmup_steps_run": rep.warm_steps,
@@ -872,7 +873,7 @@ def run_ours(args) -> int:
             "gbs": round(lm["gbs"], 1), "per_gpu_gbs": round(lm["local_gbs"], 1),
             "frac_of_peak_per_gpu": round(lm["local_gbs"] / peak, 4), "rows_per_gpu": lm["rows_local"],
             "weight_copies": lm["weight_copies"], "windows": lm["windows"], "parity": lm["parity"],
-            "parallelism": f"rows{world}+allgather", "scaling": "strong"}
+            "parallelism": f"rows{world}+allgather ({lm['exchange']})", "scaling": "strong"}
     if world == 1 and not args.no_orient:
         o = gemv_leg(args, dev, rank, world, OUT_DIM, IN_DIM, DTYPE, seed=21, K=max(K, 20), W=W)
         extra["q4k_4096x14336"] = {
@@ -893,7 +894,7 @@ def run_ours(args) -> int:
             "warmup": W, "ms_per_step": round(head["ms"] / K, 6), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": headline_config(),
-            "parallelism": "single GPU" if world == 1 else f"rows{world}+allgather (NCCL, in place)",
+            "parallelism": "single GPU" if world == 1 else f"rows{world}+allgather ({head['exchange']})",
             "weight_copies": head["weight_copies"], "weight_set_mb": head["weight_set_mb"], "l2_mb": head["l2_mb"],
             "warmup_steps_run": head["warmup_steps_run"],
             "warmup_note": "every graph the timed region replays is replayed twice first, and 256 more steps run "

@@ -157,9 +157,13 @@ M3G_API void m3g_offload_destroy(m3g_offload* ctx);
 
 /* One process per GPU.  Rank r keeps output rows [r*RPR, min(out, (r+1)*RPR))
  * of each tensor, RPR = ceil(out_dim / world); a matvec computes the local
- * rows and one NCCL all-gather of the fp32 slices gives every rank the whole
- * output.  No counterpart in the reference (it is single-host, single-CPU);
- * this is the sharded form of the GpuOffload shape above. */
+ * rows and every rank receives the whole fp32 output.  The rows travel by
+ * peer stores from the GEMV's epilogue into every rank's exchange region over
+ * NVLink (when every rank can map every other rank's region, batch 1, and the
+ * shape has a tensor-core plan; tuning key "shard_p2p", default 1), else by
+ * one in-place NCCL all-gather of the fp32 slices.  No counterpart in the
+ * reference (it is single-host, single-CPU); this is the sharded form of the
+ * GpuOffload shape above. */
 typedef struct m3g_shard m3g_shard;
 
 /* Row partition of a tensor (pure host arithmetic): M3G_ENONE when rows do
@@ -172,7 +176,9 @@ M3G_API int m3g_shard_plan(uint32_t dtype, uint64_t in_dim, uint64_t out_dim, in
 M3G_API int m3g_shard_unique_id(uint8_t* out128);
 
 /* Join the communicator; M3G_ETIMEOUT (communicator aborted) when it is not
- * complete within timeout_s seconds, e.g. because a rank never joined. */
+ * complete within timeout_s seconds, e.g. because a rank never joined.  With
+ * world > 1 it also maps the ranks' exchange regions (collective: every rank
+ * calls it with the same max_out). */
 M3G_API int m3g_shard_create(int device, int rank, int world, const uint8_t* id128, uint64_t max_in,
                              uint64_t max_out, double timeout_s, m3g_shard** out);
 
@@ -192,6 +198,8 @@ M3G_API int m3g_shard_matvec(m3g_shard* ctx, uint64_t tidx, const float* x, uint
 M3G_API int m3g_shard_info(const m3g_shard* ctx, uint64_t tidx, uint64_t* row_begin, uint64_t* rows_local,
                            uint64_t* rows_per_rank);
 M3G_API uint64_t m3g_shard_calls(const m3g_shard* ctx);
+/* How rows are exchanged: 0 one rank, 1 NCCL all-gather, 2 peer stores. */
+M3G_API int m3g_shard_exchange(const m3g_shard* ctx);
 M3G_API void m3g_shard_destroy(m3g_shard* ctx);
 
 /* ---------------------------------------------------------------- fused GEMV forms of the decode step */

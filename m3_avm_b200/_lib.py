@@ -70,6 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "m3g_shard_matvec": (ctypes.c_int, [_vp, _u64, _vp, _u64, _u64, _u64, _vp]),
     "m3g_shard_info": (ctypes.c_int, [_vp, _u64] + [ctypes.POINTER(_u64)] * 3),
     "m3g_shard_calls": (_u64, [_vp]),
+    "m3g_shard_exchange": (ctypes.c_int, [_vp]),
     "m3g_shard_destroy": (None, [_vp]),
     "m3g_matvec_fused_dev": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _u64, _u32, _u64,
                                             _u64, _vp, _vp]),

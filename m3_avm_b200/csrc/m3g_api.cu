@@ -98,6 +98,9 @@ struct Tuning {
   int64_t umma_chains = 8;        // independent accumulators per super-block (capped by TMEM)
   int64_t offload_graph = 1;      // host-buffer offload calls replay one CUDA graph (copy in, GEMV, copy out)
   int64_t peer_wait_us = 2000000; // limit of a kernel's wait for a counter bumped by other GPUs
+  int64_t mma_tail_first = 1;     // tensor-core GEMV: a CTA's partial row group first
+  int64_t offload_mapped = 1;     // batch-1 host-buffer calls: x, y, status through mapped pinned memory
+  int64_t shard_p2p = 1;          // shard contexts: rows exchanged by peer stores from the GEMV epilogue
 };
 Tuning g_tune;
 
@@ -295,6 +298,7 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   p.a.NS = static_cast<int>(NS);
   p.a.PRE = static_cast<int>(std::max<int64_t>(0, g_tune.mma_pre));
   p.a.peer_wait_ns = static_cast<unsigned long long>(g_tune.peer_wait_us) * 1000ull;
+  p.a.tail_first = g_tune.mma_tail_first ? 1 : 0;
   p.tps = tps;
   p.wk = wk;
   const long long ctas = static_cast<long long>(ds.sms) * mctas;
@@ -613,6 +617,8 @@ int gemv_fused(int device, uint32_t dtype, const uint8_t* w, uint64_t raw_len, c
     mp.a.wait_cnt = peers->wait_cnt;
     mp.a.wait_mul = peers->wait_mul;
     mp.a.key_by_step = peers->key_by_step;
+    mp.a.ystep = peers->ystep;
+    mp.a.ystride = peers->ystride;
   }
   if (grid_out) *grid_out = mp.grid;
   cudaError_t e = launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);
@@ -651,6 +657,18 @@ int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const flo
 }
 
 bool decode_p2p_enabled() { return g_tune.decode_p2p != 0; }
+bool shard_p2p_enabled() { return g_tune.shard_p2p != 0; }
+
+bool fused_plannable(int device, uint32_t dtype, long long in_dim, long long rows) {
+  FmtInfo f;
+  if (!fmt_info(dtype, f) || rows < 1) return false;
+  DevState* ds = nullptr;
+  if (dev_state(device, &ds)) return false;
+  MmaPlan mp;
+  alignas(16) static const float kAligned[4] = {0.f, 0.f, 0.f, 0.f};  // stands in for 16-byte aligned w and x
+  const uint8_t* w16 = reinterpret_cast<const uint8_t*>(kAligned);
+  return plan_mma(f, in_dim, rows, w16, kAligned, *ds, mp, false);
+}
 unsigned long long peer_wait_ns() { return static_cast<unsigned long long>(g_tune.peer_wait_us) * 1000ull; }
 bool decode_shard_ffn_enabled() { return g_tune.decode_shard_ffn != 0; }
 
@@ -708,6 +726,9 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "offload_graph")) g_tune.offload_graph = value != 0;
   else if (!strcmp(key, "umma_chains") && value >= 1 && value <= 8) g_tune.umma_chains = value;
   else if (!strcmp(key, "peer_wait_us") && value >= 1 && value <= 60000000) g_tune.peer_wait_us = value;
+  else if (!strcmp(key, "mma_tail_first")) g_tune.mma_tail_first = value != 0;
+  else if (!strcmp(key, "offload_mapped")) g_tune.offload_mapped = value != 0;
+  else if (!strcmp(key, "shard_p2p")) g_tune.shard_p2p = value != 0;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }
@@ -973,6 +994,16 @@ struct m3g_offload {
   uint8_t* h_out = nullptr;       // pinned: [status (16 bytes)][y]
   float* h_y = nullptr;           // h_out + 16
   uint32_t* h_status = nullptr;   // h_out
+  // Batch-1 calls on the tensor-core plan move x, y and the status word
+  // through mapped pinned memory instead of copy-engine transfers: a small
+  // kernel pulls x in (the GEMV's weight stream overlaps it), the GEMV stores
+  // y straight into host memory, and one store returns the status word.
+  float* hm_x = nullptr;
+  float* hm_x_dev = nullptr;
+  float* hm_y = nullptr;
+  float* hm_y_dev = nullptr;
+  uint32_t* hm_st = nullptr;
+  uint32_t* hm_st_dev = nullptr;
   uint64_t calls = 0;
   std::unordered_map<uint64_t, ResidentTensor> tensors;
   // Host-buffer calls: one captured graph per tensor (copy x in, GEMV, copy y
@@ -982,6 +1013,7 @@ struct m3g_offload {
     cudaGraphExec_t exec = nullptr;
     uint64_t batch = 0;
     const uint8_t* w = nullptr;
+    bool mapped = false;
   };
   std::unordered_map<uint64_t, HostGraph> graphs;
   bool graphs_ok = true;  // cleared if a capture ever fails: calls then run eagerly
@@ -1016,6 +1048,28 @@ void free_io(m3g_offload* c) {
   c->d_out = c->h_out = nullptr;
   c->d_status = c->h_status = nullptr;
   c->cap_batch = 0;
+}
+
+void free_mapped(m3g_offload* c) {
+  for (void* p : {static_cast<void*>(c->hm_x), static_cast<void*>(c->hm_y), static_cast<void*>(c->hm_st)})
+    if (p) cudaFreeHost(p);
+  c->hm_x = c->hm_x_dev = c->hm_y = c->hm_y_dev = nullptr;
+  c->hm_st = c->hm_st_dev = nullptr;
+}
+
+// Mapped pinned buffers of the batch-1 host call (allocated once, at create).
+int ensure_mapped(m3g_offload* c) {
+  if (c->hm_x) return M3G_OK;
+  const size_t nx = static_cast<size_t>(std::max<uint64_t>(c->max_in, 16));
+  const size_t ny = static_cast<size_t>(std::max<uint64_t>(c->max_out, 16));
+  M3G_CUDA(cudaHostAlloc(&c->hm_x, nx * sizeof(float), cudaHostAllocMapped));
+  M3G_CUDA(cudaHostAlloc(&c->hm_y, ny * sizeof(float), cudaHostAllocMapped));
+  M3G_CUDA(cudaHostAlloc(&c->hm_st, 64, cudaHostAllocMapped));
+  M3G_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->hm_x_dev), c->hm_x, 0));
+  M3G_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->hm_y_dev), c->hm_y, 0));
+  M3G_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->hm_st_dev), c->hm_st, 0));
+  *c->hm_st = 0u;
+  return M3G_OK;
 }
 
 int ensure_io(m3g_offload* c, uint64_t batch) {
@@ -1056,7 +1110,15 @@ int m3g_offload_create(int device, uint64_t max_in, uint64_t max_out, m3g_offloa
     delete c;
     return cuda_fail(e, "cudaStreamCreate");
   }
-  if (int rc = ensure_io(c, 1)) {
+  int rc = ensure_io(c, 1);
+  if (!rc && g_tune.offload_mapped) {
+    rc = ensure_mapped(c);
+    if (rc) {  // no mapped memory here: every call takes the copy path
+      free_mapped(c);
+      rc = M3G_OK;
+    }
+  }
+  if (rc) {
     free_io(c);
     cudaStreamDestroy(c->stream);
     delete c;
@@ -1073,6 +1135,7 @@ void m3g_offload_destroy(m3g_offload* c) {
   drop_graphs(c);
   for (auto& kv : c->tensors) cudaFree(kv.second.d_raw);
   free_io(c);
+  free_mapped(c);
   cudaStreamDestroy(c->stream);
   delete c;
 }
@@ -1166,17 +1229,34 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
   if (int rc = ensure_io(c, batch)) return rc;
   const size_t bx = static_cast<size_t>(in_dim * batch) * sizeof(float);
   const size_t by = static_cast<size_t>(out_dim * batch) * sizeof(float);
-  memcpy(c->h_x, x, bx);
   DevState* ds = nullptr;
   if (int rc = dev_state(c->device, &ds)) return rc;
-  // The kernels of this call report into the context's status word, which
-  // travels back in the same copy as y.
+  // The kernels of this call report into the context's status word.
   DevState dsc = *ds;
   dsc.status = c->d_status;
   FmtInfo f;
   fmt_info(t.dtype, f);
-  // copy in, GEMV, one copy out of [status | y], on c->stream
+  // Batch 1 on the tensor-core plan (plain stores of y, no atomics): x, y and
+  // the status word go through mapped pinned memory.  Otherwise: copy in,
+  // GEMV, one copy out of [status | y].
+  MmaPlan probe;
+  const bool mapped = batch == 1 && c->hm_x && g_tune.offload_mapped && in_dim % 4 == 0 && !g_tune.force_generic &&
+                      g_tune.mma && plan_mma(f, static_cast<long long>(in_dim), static_cast<long long>(out_dim),
+                                             t.d_raw, c->d_x, *ds, probe, g_tune.mma_coresident != 0);
+  memcpy(mapped ? c->hm_x : c->h_x, x, bx);
   auto enqueue = [&]() -> int {
+    if (mapped) {
+      cudaError_t e = m3g::launch_host_x_in(c->hm_x_dev, c->d_x, static_cast<long long>(in_dim), c->stream);
+      if (e != cudaSuccess) return cuda_fail(e, "x copy-in kernel");
+      if (int rc = gemv_batch_launch(dsc, f, t.d_raw, c->d_x, c->hm_y_dev, static_cast<long long>(t.in_dim),
+                                     static_cast<long long>(t.out_dim), 1, c->stream))
+        return rc;
+      ++c->calls;
+      e = m3g::launch_host_status_out(c->d_status, c->hm_st_dev, c->stream, g_tune.pdl != 0);
+      if (e != cudaSuccess) return cuda_fail(e, "status copy-out kernel");
+      g_launches.fetch_add(2, std::memory_order_relaxed);
+      return M3G_OK;
+    }
     M3G_CUDA(cudaMemcpyAsync(c->d_x, c->h_x, bx, cudaMemcpyHostToDevice, c->stream));
     if (int rc = gemv_batch_launch(dsc, f, t.d_raw, c->d_x, c->d_y, static_cast<long long>(t.in_dim),
                                    static_cast<long long>(t.out_dim), static_cast<long long>(batch), c->stream))
@@ -1188,7 +1268,8 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
   m3g_offload::HostGraph* hg = nullptr;
   if (g_tune.offload_graph && c->graphs_ok) {
     auto gi = c->graphs.find(tidx);
-    if (gi != c->graphs.end() && (gi->second.batch != batch || gi->second.w != t.d_raw)) {
+    if (gi != c->graphs.end() &&
+        (gi->second.batch != batch || gi->second.w != t.d_raw || gi->second.mapped != mapped)) {
       if (gi->second.exec) cudaGraphExecDestroy(gi->second.exec);
       c->graphs.erase(gi);
       gi = c->graphs.end();
@@ -1205,7 +1286,7 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
       if (graph) cudaGraphDestroy(graph);
       cudaGetLastError();  // a failed capture leaves no sticky error; clear the last one
       if (ok) {
-        gi = c->graphs.emplace(tidx, m3g_offload::HostGraph{exec, batch, t.d_raw}).first;
+        gi = c->graphs.emplace(tidx, m3g_offload::HostGraph{exec, batch, t.d_raw, mapped}).first;
       } else {
         if (exec) cudaGraphExecDestroy(exec);
         c->graphs_ok = false;  // run this and later calls eagerly
@@ -1220,10 +1301,11 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
     return rc;
   }
   M3G_CUDA(cudaStreamSynchronize(c->stream));
-  memcpy(y, c->h_y, by);
-  if (*c->h_status) {
-    const uint32_t bits = *c->h_status;
+  memcpy(y, mapped ? c->hm_y : c->h_y, by);
+  const uint32_t bits = mapped ? *static_cast<volatile uint32_t*>(c->hm_st) : *c->h_status;
+  if (bits) {
     cudaMemset(c->d_status, 0, sizeof(uint32_t));
+    if (mapped) *static_cast<volatile uint32_t*>(c->hm_st) = 0u;
     return fail(M3G_ETIMEOUT, "a bounded wait in the GEMV gave up (status 0x%x)", bits);
   }
   return M3G_OK;

@@ -59,6 +59,7 @@ struct MmaArgs {
   int SEG;            // bytes of one row's segment within a group
   int NS;             // stages
   int PRE;            // stages issued before the grid dependency resolves
+  int tail_first;     // 1: a CTA's partial last row group is visited first
   int rows_per_cta;
   int off_xsl, off_sum32, off_sum16, off_scale, off_red, off_bar;
   // Fused input transform and epilogue (all zero for a plain GEMV):
@@ -100,6 +101,10 @@ struct MmaArgs {
   const unsigned int* wait_cnt;
   unsigned int wait_mul;
   unsigned long long peer_wait_ns;
+  // Non-null: every peer store goes ystride floats further on when *ystep is
+  // odd (double-buffered exchange; *ystep is read after the grid dependency).
+  const int* ystep;
+  long long ystride;
   // 1: the greedy key of step *step is argmax_key[*step & 1] (and the same
   // slot of every peer_key), so that a rank one step ahead merges into the
   // other slot while this rank still reads the last one.
@@ -117,6 +122,8 @@ struct PeerIO {
   const unsigned int* wait_cnt = nullptr;
   unsigned int wait_mul = 0;
   int key_by_step = 0;
+  const int* ystep = nullptr;
+  long long ystride = 0;
 };
 
 enum XMode : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
@@ -140,6 +147,12 @@ int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const flo
 // Limit of a kernel's wait for a counter that other GPUs (or another
 // producer) bump: the tuning key peer_wait_us, 2 s by default.
 unsigned long long peer_wait_ns();
+
+// Whether a shard context may exchange rows by peer stores (tuning knob).
+bool shard_p2p_enabled();
+// Whether the tensor-core GEMV has a plan for `rows` rows of `in_dim` inputs
+// of `dtype` on `device` (16-byte aligned weights and input assumed).
+bool fused_plannable(int device, uint32_t dtype, long long in_dim, long long rows);
 
 // Whether a sharded decoder may exchange rows by peer stores (tuning knob).
 bool decode_p2p_enabled();
@@ -192,5 +205,10 @@ cudaError_t launch_gemv_stream(int fmt, const StreamArgs& a, int threads, int gr
 cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float* y, long long in_dim,
                                 long long nblocks, int grid, cudaStream_t st);
 cudaError_t launch_dequant(int fmt, const uint8_t* w, float* out, long long n_elems, int grid, cudaStream_t st);
+
+// Host-buffer GEMV I/O through mapped pinned memory (device-side aliases):
+// x in (n % 4 == 0, 16-byte aligned), and the status word out after the GEMV.
+cudaError_t launch_host_x_in(const float* hx_dev, float* dx, long long n, cudaStream_t st);
+cudaError_t launch_host_status_out(const uint32_t* dstatus, uint32_t* hstatus_dev, cudaStream_t st, bool pdl);
 
 }  // namespace m3g

@@ -467,6 +467,12 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
   const int nrows = static_cast<int>(row_end - row0);
   const int ngroups = (nrows + SR - 1) / SR;
   const int nst = ngroups * a.NKC;
+  // Row group of the s-th group visited.  With tail_first a partial last
+  // group is visited first: its tile costs as much arithmetic as a full one
+  // but little HBM time, so done early it hides behind the weight stream
+  // instead of adding its arithmetic after the last bytes arrive.
+  const bool tail_first = a.tail_first && ngroups > 1 && (nrows % SR) != 0;
+  auto group_of = [&](int v) -> int { return tail_first ? (v == 0 ? ngroups - 1 : v - 1) : v; };
 
   float* red = reinterpret_cast<float*>(smem + a.off_red);  // [NS][SR][WK]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
@@ -492,7 +498,8 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
     // CG consecutive rows (whole rows when CG > 1, since then NKC == 1).
     const size_t stage_bytes = static_cast<size_t>(SR / a.CG) * a.GS;
     auto issue = [&](int s) {
-      const int grp = s / a.NKC, kc = s - grp * a.NKC;
+      const int vis = s / a.NKC, kc = s - vis * a.NKC;
+      const int grp = group_of(vis);
       const int rows_g = min(SR, nrows - SR * grp);
       const int sb0 = kc * a.KC;
       const int seg = min(a.KC, a.NSB - sb0) * F::kSBBytes;
@@ -526,11 +533,16 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
     uint32_t ph = 0;
     bool ok = true;
     unsigned long long best_key = 0ull;  // argmax epilogue: this lane's best (value, row)
+    // Peer stores go to the half of the exchange buffers this call's parity
+    // selects (read after the grid dependency: an earlier kernel advances it).
+    long long ypar = 0;
+    if constexpr (FUSED) ypar = a.ystep ? static_cast<long long>(*a.ystep & 1) * a.ystride : 0;
     for (int s = 0; s < nst; ++s) {
       ok = mbar_wait_bounded(&empty[buf], ph, kMmaTimeoutNs, abort_flag);
       if (!ok) break;
-      const int grp = s / a.NKC;
-      if (s - grp * a.NKC == a.NKC - 1) {
+      const int vis = s / a.NKC;
+      if (s - vis * a.NKC == a.NKC - 1) {
+        const int grp = group_of(vis);
         const int rows_g = min(SR, nrows - SR * grp);
         const float* rb = red + static_cast<size_t>(buf) * SR * WK;
         float acc = 0.f;
@@ -549,13 +561,13 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
               const float h = __fmul_rn(__fdividef(acc, 1.0f + __expf(-acc)), u);
               a.y[o] = h;
               for (int p = 0; p < a.npeer; ++p)
-                if (a.peer_y[p]) a.peer_y[p][o] = h;
+                if (a.peer_y[p]) a.peer_y[p][o + ypar] = h;
             }
           } else if (lane < rows_g) {
             const float yv = a.res ? a.res[r] + acc : acc;
             a.y[r] = yv;
             for (int p = 0; p < a.npeer; ++p)
-              if (a.peer_y[p]) a.peer_y[p][r] = yv;
+              if (a.peer_y[p]) a.peer_y[p][r + ypar] = yv;
             if (a.argmax_key && yv == yv) best_key = max(best_key, argmax_key(yv, r + a.key_row0));
           }
         } else if (lane < rows_g) {

@@ -2,9 +2,19 @@
 //
 // Each rank (one process per GPU) keeps rows [r*RPR, min(out, (r+1)*RPR)) of
 // a weight tensor resident, RPR = ceil(out_dim / world).  A matvec computes
-// the local rows with the single-GPU kernels straight into this rank's slot
-// of a gather buffer, then one NCCL all-gather (in place) gives every rank
-// the full fp32 output.  This is the only collective of the path.
+// the local rows straight into this rank's slot of the gather buffer, and the
+// other ranks' slots arrive in one of two ways:
+//
+//  * peer stores (default when every rank can map every other rank's
+//    exchange region over NVLink): the GEMV's epilogue stores each row into
+//    every peer's exchange region as well, and the CTA that completes the
+//    rank's rows adds 1 to every peer's arrival counter after a system-scope
+//    fence -- the all-gather is fused into the GEMV, tile by tile.  A small
+//    kernel then waits (bounded) for all ranks' arrivals and copies the
+//    peers' slots into the caller's buffer.  The regions are double-buffered
+//    by call parity, so a rank one call ahead never overwrites rows a peer
+//    still copies;
+//  * otherwise one in-place NCCL all-gather of the fp32 slices.
 //
 // Communicator creation is non-blocking with a wall-clock limit: a rank that
 // never joins makes create() abort the communicator and return M3G_ETIMEOUT
@@ -13,11 +23,13 @@
 #include <cstring>
 #include <thread>
 #include <unordered_map>
+#include <vector>
 
 #include <cuda_runtime.h>
 #include <nccl.h>
 
 #include "../../include/m3gemv.h"
+#include "m3g_device.cuh"
 #include "m3g_internal.h"
 
 namespace m3g {
@@ -127,9 +139,133 @@ struct m3g_shard {
   uint64_t cap_x = 0, cap_ws = 0;
   uint64_t calls = 0;
   double timeout_s = 60.0;
+  // Peer-store exchange: this rank's region (counters, then two halves of
+  // world * rpr_cap floats) and every rank's region mapped here.
+  bool p2p = false;
+  uint8_t* region = nullptr;
+  uint8_t* peer_base[m3g::kMaxPeers] = {};
+  uint64_t rpr_cap = 0;  // rows per rank the region holds
 };
 
 namespace {
+
+// Exchange region layout: counters first (a peer adds to arr), then the two
+// halves of the gathered rows.
+constexpr size_t kArrOff = 0;     // u32: arrivals (every rank adds 1 per call)
+constexpr size_t kDoneOff = 64;   // u32: this rank's GEMV CTAs done in this call
+constexpr size_t kStepOff = 128;  // i32: calls completed (parity of the halves)
+constexpr size_t kZeroOff = 192;  // i32: constant 0 (the GEMV's per-call count base)
+constexpr size_t kFinOff = 256;   // u32: gather CTAs finished in this call
+constexpr size_t kRowsOff = 512;  // f32 [2][world * rpr_cap]
+
+// Waits (bounded) until every rank's rows of this call have arrived, copies
+// the other ranks' slots from this call's half of the region into y (this
+// rank's slot is already there), and closes the call: the last CTA clears the
+// per-call counts and advances the step.
+__global__ void __launch_bounds__(256) k_shard_gather(uint8_t* region, unsigned world, int rank, long long rpr,
+                                                      long long rpr_cap, float* __restrict__ y, long long n,
+                                                      uint32_t* status, unsigned long long wait_ns) {
+  m3g::grid_dep_wait();
+  const unsigned* arr = reinterpret_cast<const unsigned*>(region + kArrOff);
+  int* step = reinterpret_cast<int*>(region + kStepOff);
+  __shared__ int s_step;
+  if (threadIdx.x == 0) {
+    const int s = *reinterpret_cast<volatile int*>(step);
+    const unsigned target = static_cast<unsigned>(s + 1) * world;
+    if (!m3g::wait_count_bounded(arr, target, wait_ns)) atomicOr(status, m3g::kStatusPeerTimeout);
+    s_step = s;
+  }
+  __syncthreads();
+  const int s = s_step;
+  const float* src = reinterpret_cast<const float*>(region + kRowsOff) + static_cast<long long>(s & 1) * world * rpr_cap;
+  const long long mine0 = static_cast<long long>(rank) * rpr, mine1 = mine0 + rpr;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    if (i >= mine0 && i < mine1) continue;
+    y[i] = __ldcg(src + (i / rpr) * rpr_cap + i % rpr);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned* fin = reinterpret_cast<unsigned*>(region + kFinOff);
+    if (atomicAdd(fin, 1u) == gridDim.x - 1) {
+      *fin = 0u;
+      *reinterpret_cast<unsigned*>(region + kDoneOff) = 0u;
+      *step = s + 1;
+      __threadfence();
+    }
+  }
+}
+
+// Maps every rank's exchange region (CUDA IPC over NVLink): handles are
+// swapped with one NCCL all-gather and the ranks agree (MIN all-reduce) that
+// every mapping opened; otherwise every rank keeps the NCCL path.
+int open_peer_regions(m3g_shard* c) {
+  c->p2p = false;
+  c->peer_base[c->rank] = c->region;
+  constexpr int kRec = 72;  // 64-byte handle + ok flag
+  uint8_t rec[kRec] = {};
+  cudaIpcMemHandle_t mine;
+  memset(&mine, 0, sizeof mine);
+  int ok = c->region && cudaIpcGetMemHandle(&mine, c->region) == cudaSuccess ? 1 : 0;
+  cudaGetLastError();
+  memcpy(rec, &mine, sizeof mine);
+  memcpy(rec + 64, &ok, sizeof ok);
+  uint8_t* dev = nullptr;
+  cudaError_t e = cudaMalloc(&dev, static_cast<size_t>(kRec) * c->world + 16);
+  if (e != cudaSuccess) return m3g::host_fail(M3G_ENOMEM, "peer handles: %s", cudaGetErrorString(e));
+  std::vector<uint8_t> all(static_cast<size_t>(kRec) * c->world);
+  int rc = M3G_OK;
+  e = cudaMemcpy(dev + kRec * c->rank, rec, kRec, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    rc = nccl_settle(c->comm, ncclAllGather(dev + kRec * c->rank, dev, kRec, ncclUint8, c->comm, c->stream),
+                     "ncclAllGather(ipc handles)", c->timeout_s);
+    if (!rc) e = cudaStreamSynchronize(c->stream);
+    if (!rc && e == cudaSuccess) e = cudaMemcpy(all.data(), dev, all.size(), cudaMemcpyDeviceToHost);
+  }
+  if (rc || e != cudaSuccess) {
+    cudaFree(dev);
+    return rc ? rc : m3g::host_fail(M3G_ECUDA, "peer handle exchange: %s", cudaGetErrorString(e));
+  }
+  int mine_ok = 1;
+  for (int p = 0; p < c->world; ++p) {
+    int okp = 0;
+    memcpy(&okp, all.data() + kRec * p + 64, sizeof okp);
+    if (!okp) mine_ok = 0;
+  }
+  for (int p = 0; p < c->world && mine_ok; ++p) {
+    if (p == c->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, all.data() + kRec * p, sizeof h);
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      mine_ok = 0;
+      break;
+    }
+    c->peer_base[p] = static_cast<uint8_t*>(ptr);
+  }
+  int* flag = reinterpret_cast<int*>(dev);
+  e = cudaMemcpy(flag, &mine_ok, sizeof mine_ok, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    rc = nccl_settle(c->comm, ncclAllReduce(flag, flag, 1, ncclInt, ncclMin, c->comm, c->stream),
+                     "ncclAllReduce(peer agreement)", c->timeout_s);
+    if (!rc) e = cudaStreamSynchronize(c->stream);
+  }
+  int all_ok = 0;
+  if (!rc && e == cudaSuccess) e = cudaMemcpy(&all_ok, flag, sizeof all_ok, cudaMemcpyDeviceToHost);
+  cudaFree(dev);
+  if (!rc && e == cudaSuccess && all_ok) {
+    c->p2p = true;
+    return M3G_OK;
+  }
+  for (int p = 0; p < c->world; ++p)
+    if (p != c->rank && c->peer_base[p]) cudaIpcCloseMemHandle(c->peer_base[p]);
+  for (int p = 0; p < c->world; ++p) c->peer_base[p] = p == c->rank ? c->region : nullptr;
+  if (rc) return rc;
+  if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "peer agreement: %s", cudaGetErrorString(e));
+  return M3G_OK;
+}
 
 struct Dev {
   int prev = -1;
@@ -213,6 +349,33 @@ int m3g_shard_create(int device, int rank, int world, const uint8_t* id128, uint
     delete c;
     return m3g::host_fail(M3G_ECUDA, "cudaStreamCreate: %s", cudaGetErrorString(e));
   }
+  // The device's kernel state (status word, SM count) is made now, so that a
+  // later matvec may be captured into a CUDA graph (no allocation inside it).
+  uint32_t* status = nullptr;
+  if (int rc = m3g::status_word(device, &status)) {
+    cudaStreamDestroy(c->stream);
+    ncclCommAbort(c->comm);
+    delete c;
+    return rc;
+  }
+  // Peer-store exchange region.  Every rank makes the same decision (the
+  // tuning key is process-wide) and joins the collective agreement, even one
+  // whose allocation failed: it then votes no and every rank keeps NCCL.
+  if (world > 1 && world <= m3g::kMaxPeers && m3g::shard_p2p_enabled()) {
+    c->rpr_cap = (max_out + world - 1) / world;
+    const size_t bytes = kRowsOff + 2 * static_cast<size_t>(world) * c->rpr_cap * sizeof(float);
+    cudaError_t ea = cudaMalloc(&c->region, bytes);
+    if (ea == cudaSuccess) ea = cudaMemset(c->region, 0, kRowsOff);
+    if (ea != cudaSuccess) {
+      cudaGetLastError();
+      if (c->region) cudaFree(c->region);
+      c->region = nullptr;
+    }
+    if (int rc = open_peer_regions(c)) {
+      m3g_shard_destroy(c);
+      return rc;
+    }
+  }
   *out = c;
   return M3G_OK;
 }
@@ -221,6 +384,19 @@ void m3g_shard_destroy(m3g_shard* c) {
   if (!c) return;
   Dev g(c->device);
   cudaDeviceSynchronize();
+  if (c->p2p && c->comm) {
+    // no rank may unmap or free a region while another still stores into it
+    int* one = nullptr;
+    if (cudaMalloc(&one, sizeof(int)) == cudaSuccess) {
+      if (nccl_settle(c->comm, ncclAllReduce(one, one, 1, ncclInt, ncclSum, c->comm, c->stream),
+                      "ncclAllReduce(teardown barrier)", c->timeout_s) == M3G_OK)
+        cudaStreamSynchronize(c->stream);
+      cudaFree(one);
+    }
+  }
+  for (int p = 0; p < c->world && p < m3g::kMaxPeers; ++p)
+    if (p != c->rank && c->peer_base[p]) cudaIpcCloseMemHandle(c->peer_base[p]);
+  if (c->region) cudaFree(c->region);
   for (auto& kv : c->tensors) cudaFree(kv.second.d_raw);
   if (c->d_x) cudaFree(c->d_x);
   if (c->d_ws) cudaFree(c->d_ws);
@@ -282,6 +458,47 @@ int m3g_shard_matvec_dev(m3g_shard* c, uint64_t tidx, const float* x, uint64_t b
   Dev g(c->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL: the legacy default stream
   float* slot = y + static_cast<uint64_t>(c->rank) * batch * t.rpr;
+  // The peer-store form needs every rank to hold rows and a tensor-core plan
+  // for the shape; both depend only on the tensor, so every rank decides alike.
+  const bool p2p = c->p2p && batch == 1 && t.rpr <= c->rpr_cap &&
+                   static_cast<uint64_t>(c->world - 1) * t.rpr < t.out_dim &&
+                   m3g::fused_plannable(c->device, t.dtype, static_cast<long long>(t.in_dim),
+                                        static_cast<long long>(t.rows_local));
+  if (p2p) {
+    const float* xin = x;
+    if (reinterpret_cast<uintptr_t>(x) % 16) {  // the tensor-core plan reads x 16 bytes at a time
+      if (int rc = grow(&c->d_x, &c->cap_x, t.in_dim)) return rc;
+      cudaError_t e = cudaMemcpyAsync(c->d_x, x, t.in_dim * sizeof(float), cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard x copy: %s", cudaGetErrorString(e));
+      xin = c->d_x;
+    }
+    m3g::PeerIO io;
+    for (int p = 0; p < c->world; ++p) {
+      io.peer_cnt[p] = reinterpret_cast<unsigned int*>(c->peer_base[p] + kArrOff);
+      if (p != c->rank)
+        io.peer_y[p] = reinterpret_cast<float*>(c->peer_base[p] + kRowsOff) + static_cast<uint64_t>(c->rank) * c->rpr_cap;
+    }
+    io.npeer = c->world;
+    io.done_cnt = reinterpret_cast<unsigned int*>(c->region + kDoneOff);
+    io.step = reinterpret_cast<const int*>(c->region + kZeroOff);
+    io.ystep = reinterpret_cast<const int*>(c->region + kStepOff);
+    io.ystride = static_cast<long long>(c->world) * static_cast<long long>(c->rpr_cap);
+    if (int rc = m3g::gemv_fused(c->device, t.dtype, t.d_raw, t.bytes_local, xin, nullptr, nullptr, nullptr,
+                                 m3g::kXPlain, slot, static_cast<long long>(t.in_dim),
+                                 static_cast<long long>(t.rows_local), st, false, nullptr, false, 0, &io))
+      return rc;
+    uint32_t* status = nullptr;
+    if (int rc = m3g::status_word(c->device, &status)) return rc;
+    const long long n = static_cast<long long>(c->world) * static_cast<long long>(t.rpr);
+    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(64, (n + 4095) / 4096)));
+    k_shard_gather<<<grid, 256, 0, st>>>(c->region, static_cast<unsigned>(c->world), c->rank,
+                                         static_cast<long long>(t.rpr), static_cast<long long>(c->rpr_cap), y, n,
+                                         status, m3g::peer_wait_ns());
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard gather launch: %s", cudaGetErrorString(e));
+    ++c->calls;
+    return M3G_OK;
+  }
   if (t.rows_local) {
     for (uint64_t b = 0; b < batch; ++b) {
       int rc = m3g::gemv_device(c->device, t.dtype, t.d_raw, t.bytes_local, x + b * t.in_dim, slot + b * t.rpr,
@@ -339,5 +556,11 @@ int m3g_shard_info(const m3g_shard* c, uint64_t tidx, uint64_t* row_begin, uint6
 }
 
 uint64_t m3g_shard_calls(const m3g_shard* c) { return c ? c->calls : 0; }
+
+int m3g_shard_exchange(const m3g_shard* c) {
+  if (!c) return 0;
+  if (c->world == 1) return 0;
+  return c->p2p ? 2 : 1;
+}
 
 }  // extern "C"

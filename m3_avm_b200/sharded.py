@@ -2,7 +2,9 @@
 
 Rank r of `world` keeps output rows [r*RPR, min(out, (r+1)*RPR)) of each
 tensor, RPR = ceil(out_dim / world); ``matvec`` computes the local rows and
-one NCCL all-gather gives every rank the full fp32 output.  This is the
+every rank receives the full fp32 output: by peer stores from the GEMV
+epilogue over NVLink where the ranks can map each other's exchange regions
+(``exchange == "peer-stores"``), else by one NCCL all-gather.  This is the
 multi-GPU form of the resident-weight offload (``inference_gpu.GpuOffload``);
 the reference runs on one host CPU and has no counterpart.
 """
@@ -93,6 +95,12 @@ class ShardedOffload:
     @property
     def calls(self) -> int:
         return int(_lib.load().m3g_shard_calls(self._h))
+
+    @property
+    def exchange(self) -> str:
+        """'single' (one rank), 'nccl' (in-place all-gather) or 'peer-stores'
+        (rows stored into every rank's region from the GEMV epilogue)."""
+        return {0: "single", 1: "nccl", 2: "peer-stores"}.get(int(_lib.load().m3g_shard_exchange(self._h)), "?")
 
     def close(self) -> None:
         if self._h and self._h.value:

@@ -397,3 +397,32 @@ def test_offload_replayed_calls_follow_reuploads_and_batch_sizes(m3):
     finally:
         m3.matvec_quant.set_tuning("offload_graph", 1)
     g.close()
+
+
+def test_offload_mapped_and_copy_paths_agree(m3):
+    """Batch-1 host calls on the tensor-core plan move x, y and the status word
+    through mapped pinned memory; the copy-engine path (offload_mapped 0) and
+    the non-tensor-core shapes keep the staged copies.  Same kernel, so the
+    two paths give the same bits, and both match the oracle."""
+    g = m3.inference_gpu.GpuOffload.try_new(4096, 2048)
+    assert g is not None
+    raw = m3.synth.weights(12, 4096, 2048, seed=71)
+    raw_odd = m3.synth.weights(8, 4000, 100, seed=72)  # in_dim % 256 != 0: no tensor-core plan
+    x = m3.synth.activations(4096, seed=73)
+    xo = m3.synth.activations(4000, seed=74)
+    assert g.upload(1, 12, raw, 4096, 2048) and g.upload(2, 8, raw_odd, 4000, 100)
+    ys = {}
+    for mapped in (1, 0, 1):
+        m3.matvec_quant.set_tuning("offload_mapped", mapped)
+        try:
+            for _ in range(2):  # eager capture, then the replayed graph
+                y = g.matvec(1, x, 4096, 2048)
+                check_gemv(y, raw, 12, 4096, 2048, x)
+                ys.setdefault(mapped, y.copy())
+                assert np.array_equal(y.view(np.uint32), ys[mapped].view(np.uint32))
+                check_gemv(g.matvec(2, xo, 4000, 100), raw_odd, 8, 4000, 100, xo)
+        finally:
+            m3.matvec_quant.set_tuning("offload_mapped", 1)
+    assert np.array_equal(ys[0].view(np.uint32), ys[1].view(np.uint32))
+    assert m3.matvec_quant.device_status(0) == 0
+    g.close()
