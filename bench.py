@@ -176,7 +176,8 @@ def dist_env():
 
 
 # ---------------------------------------------------------------- CPU reference timing
-def cpu_gemv_timing(threads: int, steps: int, step_s: float, warm_s: float = 2.0) -> dict:
+def cpu_gemv_timing(threads: int, steps: int, step_s: float, warm_s: float = 2.0, dtype: int = DTYPE,
+                    in_dim: int = IN_DIM, out_dim: int = OUT_DIM) -> dict:
     """The oracle's port of the reference AVX2 matvec_q4k on this host's cores.
 
     Used by both the reference arm and the CPU-baseline leg, so the two time
@@ -189,15 +190,15 @@ def cpu_gemv_timing(threads: int, steps: int, step_s: float, warm_s: float = 2.0
     from oracle import oracle as O
     from m3_avm_b200 import synth
 
-    raw = synth.weights(DTYPE, IN_DIM, OUT_DIM, seed=1)
-    x = synth.activations(IN_DIM, seed=2)
+    raw = synth.weights(dtype, in_dim, out_dim, seed=1)
+    x = synth.activations(in_dim, seed=2)
     n_copies = int(min(16, max(2, math.ceil(3 * host_llc_bytes() / raw.size))))
     copies = [raw] + [raw.copy() for _ in range(n_copies - 1)]
     calls = 0
     t_end = time.perf_counter() + warm_s
     t0 = time.perf_counter()
     while True:
-        O.matvec_quant(x, copies[calls % n_copies], DTYPE, IN_DIM, OUT_DIM, threads=threads)
+        O.matvec_quant(x, copies[calls % n_copies], dtype, in_dim, out_dim, threads=threads)
         calls += 1
         if time.perf_counter() >= t_end and calls >= 3:
             break
@@ -208,15 +209,17 @@ def cpu_gemv_timing(threads: int, steps: int, step_s: float, warm_s: float = 2.0
     for _ in range(steps):
         t0 = time.perf_counter()
         for _ in range(reps):
-            O.matvec_quant(x, copies[i % n_copies], DTYPE, IN_DIM, OUT_DIM, threads=threads)
+            O.matvec_quant(x, copies[i % n_copies], dtype, in_dim, out_dim, threads=threads)
             i += 1
         per_step.append(time.perf_counter() - t0)
     total = sum(per_step)
     per_gemv = total / (steps * reps)
-    gbs = algorithmic_bytes(IN_DIM, OUT_DIM, DTYPE) / per_gemv / 1e9
+    gbs = algorithmic_bytes(in_dim, out_dim, dtype) / per_gemv / 1e9
+    name = {12: "Q4_K", 14: "Q6_K", 8: "Q8_0", 2: "Q4_0"}[dtype]
+    kernel = "AVX2 matvec_q4k" if dtype == 12 else "matvec_blocked"
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} steps x {reps} full {OUT_DIM}x{IN_DIM} Q4_K GEMVs over {n_copies} rotating weight "
-                      f"copies (C restatement of the reference AVX2 matvec_q4k, {threads} OpenMP threads) after "
+            "sample": f"{steps} steps x {reps} full {out_dim}x{in_dim} {name} GEMVs over {n_copies} rotating weight "
+                      f"copies (C restatement of the reference {kernel}, {threads} OpenMP threads) after "
                       f"{warm_s:.0f} s of warm-up; {per_gemv * 1e3:.3f} ms per GEMV over {total:.1f} s",
             "ms_per_gemv": round(per_gemv * 1e3, 4), "gemvs_per_step": reps, "seconds": round(total, 2),
             "per_step_s": per_step}
@@ -470,6 +473,27 @@ def cpu_decode_rate(shape, tensors, prompt, n_tokens: int = 3) -> dict:
             "sample": f"{n_tokens} forward_one steps after a first step of {first:.2f} s (C restatement of "
                       f"RealInference::forward_one with matvec_quant and the f32-cached head, {threads} OpenMP "
                       f"threads), median {med * 1e3:.1f} ms"}
+
+
+def run_cpu_table(args) -> int:
+    """The reference CPU path of every single-GEMV config on this host (one
+    line per config, timed as the CPU-baseline leg)."""
+    threads = host_threads()
+    out = {}
+    for name, (dt, i, o) in {"c0 Q4_K 4096x4096": (12, 4096, 4096), "c1 Q4_K 14336x4096": (12, 4096, 14336),
+                             "c1 Q6_K 4096x14336": (14, 14336, 4096), "c1 Q8_0 4096x4096": (8, 4096, 4096),
+                             "c2 Q6_K 128256x4096": (14, 4096, 128256)}.items():
+        r = cpu_gemv_timing(threads, steps=4, step_s=1.0, warm_s=1.0, dtype=dt, in_dim=i, out_dim=o)
+        r.pop("per_step_s", None)
+        out[name] = {"gbs": r["value"], "ms_per_gemv": r["ms_per_gemv"], "cores": threads}
+    cpu = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            cpu = next(l.split(":", 1)[1].strip() for l in f if l.startswith("model name"))
+    except (OSError, StopIteration):
+        pass
+    print(json.dumps({"cpu_table": out, "cpu_model": cpu, "threads": threads}), flush=True)
+    return 0
 
 
 def run_reference(args) -> int:
@@ -839,8 +863,21 @@ def run_ours(args) -> int:
     sampler.start()
 
     K, W = args.steps, args.warmup
-    head = gemv_leg(args, dev, rank, world, IN_DIM, OUT_DIM, DTYPE, seed=1, K=K, W=W,
-                    e2e_steps=0 if args.no_e2e else min(K * 10, 5000) if K < 500 else min(K, 5000))
+    e2e_steps = 0 if args.no_e2e else min(K * 10, 5000) if K < 500 else min(K, 5000)
+    head = gemv_leg(args, dev, rank, world, IN_DIM, OUT_DIM, DTYPE, seed=1, K=K, W=W, e2e_steps=e2e_steps)
+    head_modes = None
+    if world > 1:
+        # the other exchange: rows stored into every rank's region by the GEMV epilogue
+        from m3_avm_b200 import matvec_quant as MQ
+
+        MQ.set_tuning("shard_p2p", 1)
+        alt = gemv_leg(args, dev, rank, world, IN_DIM, OUT_DIM, DTYPE, seed=1, K=K, W=W)
+        MQ.set_tuning("shard_p2p", 0)
+        head_modes = {m["exchange"]: {"us_per_step": round(m["per_step_s"] * 1e6, 3), "gbs": round(m["gbs"], 1),
+                                      "parity_ranks_ok": m["parity"]["ranks_ok"]} for m in (head, alt)}
+        if alt["per_step_s"] < head["per_step_s"]:
+            alt["e2e"] = head.get("e2e")
+            head = alt
     clocks = sampler.stop()
     value = head["gbs"]
     per_gpu = head["local_gbs"]
@@ -867,13 +904,26 @@ def run_ours(args) -> int:
     if not args.no_lmhead:
         lm = gemv_leg(args, dev, rank, world, HEAD_IN, HEAD_OUT, HEAD_DTYPE, seed=11, K=max(K, 20), W=W,
                       sharded_always=True)
+        lm_modes = None
+        if world > 1:
+            from m3_avm_b200 import matvec_quant as MQ
+
+            MQ.set_tuning("shard_p2p", 1)
+            lm_alt = gemv_leg(args, dev, rank, world, HEAD_IN, HEAD_OUT, HEAD_DTYPE, seed=11, K=max(K, 20), W=W,
+                              sharded_always=True)
+            MQ.set_tuning("shard_p2p", 0)
+            lm_modes = {m["exchange"]: {"us_per_step": round(m["per_step_s"] * 1e6, 3),
+                                        "parity_ranks_ok": m["parity"]["ranks_ok"]} for m in (lm, lm_alt)}
+            if lm_alt["per_step_s"] < lm["per_step_s"]:
+                lm = lm_alt
         extra["lmhead"] = {
             "workload": "q6k_lmhead_128256x4096, rows sharded over the GPUs + in-place NCCL all-gather of the fp32 "
                         "logits", "us_per_step": round(lm["per_step_s"] * 1e6, 2),
             "gbs": round(lm["gbs"], 1), "per_gpu_gbs": round(lm["local_gbs"], 1),
             "frac_of_peak_per_gpu": round(lm["local_gbs"] / peak, 4), "rows_per_gpu": lm["rows_local"],
             "weight_copies": lm["weight_copies"], "windows": lm["windows"], "parity": lm["parity"],
-            "parallelism": f"rows{world}+allgather ({lm['exchange']})", "scaling": "strong"}
+            "parallelism": f"rows{world}+allgather ({lm['exchange']})", "scaling": "strong",
+            "exchange_modes": lm_modes}
     if world == 1 and not args.no_orient:
         o = gemv_leg(args, dev, rank, world, OUT_DIM, IN_DIM, DTYPE, seed=21, K=max(K, 20), W=W)
         extra["q4k_4096x14336"] = {
@@ -907,6 +957,7 @@ def run_ours(args) -> int:
             "gpu_launches": head["gpu_launches"],
             "per_step_windows": head["windows"],
             "parity": head["parity"],
+            "exchange_modes": head_modes,
             "timing": "CUDA events around CUDA-graph replays of the steps, max over ranks" if not args.no_graph
                       else "CUDA events around host-launched steps, max over ranks",
             "clocks": clocks,
@@ -1060,15 +1111,18 @@ def main() -> int:
     ap.add_argument("--no-batched", action="store_true", help="skip the batched Q4_K 28672x8192 sweep")
     ap.add_argument("--no-lmhead", action="store_true", help="skip the sharded Q6_K vocab-head leg")
     ap.add_argument("--no-orient", action="store_true", help="skip the 4096x14336 orientation (1 GPU)")
-    ap.add_argument("--workload", choices=["gemv", "decode", "batched"], default="gemv",
+    ap.add_argument("--workload", choices=["gemv", "decode", "batched", "cpu-table"], default="gemv",
                     help="gemv: the Q4_K 14336x4096 GEMV (row-sharded + all-gather under torchrun) with the "
                          "lm_head, decode and batched legs; decode: the 1B decode alone (--steps tokens); "
-                         "batched: one Q4_K 28672x8192 GEMM")
+                         "batched: one Q4_K 28672x8192 GEMM; cpu-table: the reference CPU path of every "
+                         "single-GEMV config on this host")
     ap.add_argument("--batch", type=int, default=8, help="columns of X for --workload batched")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "cpu-table":
+        return run_cpu_table(args)
     if args.workload == "decode":
         return run_decode(args)
     if args.workload == "batched":

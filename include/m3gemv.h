@@ -157,11 +157,11 @@ M3G_API void m3g_offload_destroy(m3g_offload* ctx);
 
 /* One process per GPU.  Rank r keeps output rows [r*RPR, min(out, (r+1)*RPR))
  * of each tensor, RPR = ceil(out_dim / world); a matvec computes the local
- * rows and every rank receives the whole fp32 output.  The rows travel by
- * peer stores from the GEMV's epilogue into every rank's exchange region over
- * NVLink (when every rank can map every other rank's region, batch 1, and the
- * shape has a tensor-core plan; tuning key "shard_p2p", default 1), else by
- * one in-place NCCL all-gather of the fp32 slices.  No counterpart in the
+ * rows and every rank receives the whole fp32 output: by one in-place NCCL
+ * all-gather of the fp32 slices, or -- tuning key "shard_p2p" set to 1 before
+ * creation, batch 1, a tensor-core plan for the shape, and every rank able to
+ * map every other rank's region -- by peer stores from the GEMV's epilogue
+ * into every rank's exchange region over NVLink.  No counterpart in the
  * reference (it is single-host, single-CPU); this is the sharded form of the
  * GpuOffload shape above. */
 typedef struct m3g_shard m3g_shard;
@@ -372,7 +372,11 @@ M3G_API uint64_t m3g_launch_count(void);
  * "max_stages"), "force_generic" (route every GEMV through the
  * row-straddling generic kernel) and "peer_wait_us" (limit, in microseconds,
  * of a kernel's wait for a counter bumped by another GPU or producer; default
- * 2000000; read when a GEMV is enqueued or a decode step captured).
+ * 2000000; read when a GEMV is enqueued or a decode step captured), "tc8"
+ * (1: batch-1 Q4_K GEMVs with in_dim <= 4096 on the tcgen05 kind::i8 kernel;
+ * default 0, the mma.sync kernel being faster), "shard_p2p" (see
+ * m3g_shard_create) and "offload_mapped" (1, default: host-buffer offload
+ * calls through mapped pinned memory; 0: explicit copies).
  * Process-wide; M3G_ENONE for an unknown key or out-of-range value.  No
  * counterpart in the reference. */
 M3G_API int m3g_set_tuning(const char* key, int64_t value);

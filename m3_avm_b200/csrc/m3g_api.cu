@@ -100,7 +100,8 @@ struct Tuning {
   int64_t peer_wait_us = 2000000; // limit of a kernel's wait for a counter bumped by other GPUs
   int64_t mma_tail_first = 1;     // tensor-core GEMV: a CTA's partial row group first
   int64_t offload_mapped = 1;     // batch-1 host-buffer calls: x, y, status through mapped pinned memory
-  int64_t shard_p2p = 1;          // shard contexts: rows exchanged by peer stores from the GEMV epilogue
+  int64_t shard_p2p = 0;          // shard contexts: rows exchanged by peer stores from the GEMV epilogue (else NCCL)
+  int64_t tc8 = 0;                // batch-1 Q4_K GEMV on tcgen05 kind::i8 (k_tc8_q4k, K <= 4096); slower than mma.sync
 };
 Tuning g_tune;
 
@@ -111,6 +112,10 @@ struct DevState {
   int smem_per_sm = 0;
   int smem_optin = 0;
   uint32_t* status = nullptr;
+  // Set only in a per-call copy: the tensor-core GEMV's last CTA stores the
+  // status word to *status_host (mapped host memory), counting CTAs in *fin_cnt.
+  uint32_t* status_host = nullptr;
+  unsigned int* fin_cnt = nullptr;
 };
 std::mutex g_dev_mu;
 std::vector<DevState> g_dev;
@@ -311,12 +316,27 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
 // y[out_dim] = W x on `st`; w/x/y device pointers.
 int gemv_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const float* x, float* y,
                 long long in_dim, long long out_dim, cudaStream_t st) {
+  m3g::Tc8Plan tp;
+  if (!g_tune.force_generic && g_tune.mma && g_tune.tc8 && f.fmt == 12 &&
+      m3g::plan_tc8(in_dim, out_dim, w, x, ds.sms, ds.smem_optin, tp)) {
+    tp.a.x = x;
+    tp.a.y = y;
+    tp.a.status = ds.status;
+    tp.a.status_host = ds.status_host;
+    tp.a.fin_cnt = ds.fin_cnt;
+    cudaError_t e = m3g::launch_tc8(tp, w, st, g_tune.pdl != 0);
+    if (e != cudaSuccess) return cuda_fail(e, "k_tc8_q4k launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return M3G_OK;
+  }
   MmaPlan mp;
   if (!g_tune.force_generic && g_tune.mma && plan_mma(f, in_dim, out_dim, w, x, ds, mp, g_tune.mma_coresident != 0)) {
     mp.a.w = w;
     mp.a.x = x;
     mp.a.y = y;
     mp.a.status = ds.status;
+    mp.a.status_host = ds.status_host;
+    mp.a.fin_cnt = ds.fin_cnt;
     mp.a.xfirst = static_cast<int>(g_tune.mma_xfirst);
     cudaError_t e = m3g::launch_gemv_mma(f.fmt, mp.a, mp.tps, mp.wk, mp.grid, mp.smem, st, g_tune.pdl != 0);
     if (e != cudaSuccess) return cuda_fail(e, "k_gemv_mma launch");
@@ -729,6 +749,7 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "mma_tail_first")) g_tune.mma_tail_first = value != 0;
   else if (!strcmp(key, "offload_mapped")) g_tune.offload_mapped = value != 0;
   else if (!strcmp(key, "shard_p2p")) g_tune.shard_p2p = value != 0;
+  else if (!strcmp(key, "tc8")) g_tune.tc8 = value != 0;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }
@@ -997,7 +1018,7 @@ struct m3g_offload {
   // Batch-1 calls on the tensor-core plan move x, y and the status word
   // through mapped pinned memory instead of copy-engine transfers: a small
   // kernel pulls x in (the GEMV's weight stream overlaps it), the GEMV stores
-  // y straight into host memory, and one store returns the status word.
+  // y straight into host memory, and its last CTA stores the status word.
   float* hm_x = nullptr;
   float* hm_x_dev = nullptr;
   float* hm_y = nullptr;
@@ -1021,11 +1042,13 @@ struct m3g_offload {
 
 namespace {
 
+// Makes `dev` current for the scope; a no-op (one query) when it already is.
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
     if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    cudaSetDevice(dev);
+    if (prev == dev) prev = -1;
+    else cudaSetDevice(dev);
   }
   ~DeviceGuard() {
     if (prev >= 0) cudaSetDevice(prev);
@@ -1236,6 +1259,9 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
   dsc.status = c->d_status;
   FmtInfo f;
   fmt_info(t.dtype, f);
+  DevState dsm = dsc;  // mapped path: the GEMV's last CTA returns the status word itself
+  dsm.status_host = c->hm_st_dev;
+  dsm.fin_cnt = reinterpret_cast<unsigned int*>(c->d_out + 4);
   // Batch 1 on the tensor-core plan (plain stores of y, no atomics): x, y and
   // the status word go through mapped pinned memory.  Otherwise: copy in,
   // GEMV, one copy out of [status | y].
@@ -1248,13 +1274,11 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
     if (mapped) {
       cudaError_t e = m3g::launch_host_x_in(c->hm_x_dev, c->d_x, static_cast<long long>(in_dim), c->stream);
       if (e != cudaSuccess) return cuda_fail(e, "x copy-in kernel");
-      if (int rc = gemv_batch_launch(dsc, f, t.d_raw, c->d_x, c->hm_y_dev, static_cast<long long>(t.in_dim),
+      if (int rc = gemv_batch_launch(dsm, f, t.d_raw, c->d_x, c->hm_y_dev, static_cast<long long>(t.in_dim),
                                      static_cast<long long>(t.out_dim), 1, c->stream))
         return rc;
       ++c->calls;
-      e = m3g::launch_host_status_out(c->d_status, c->hm_st_dev, c->stream, g_tune.pdl != 0);
-      if (e != cudaSuccess) return cuda_fail(e, "status copy-out kernel");
-      g_launches.fetch_add(2, std::memory_order_relaxed);
+      g_launches.fetch_add(1, std::memory_order_relaxed);
       return M3G_OK;
     }
     M3G_CUDA(cudaMemcpyAsync(c->d_x, c->h_x, bx, cudaMemcpyHostToDevice, c->stream));

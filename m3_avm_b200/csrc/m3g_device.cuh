@@ -163,4 +163,42 @@ __device__ __forceinline__ void named_bar_arrive(int id, int count) {
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// x -> three int8 slices of super-block sb and its group sums; lane holds
+// elements 8*lane .. 8*lane+7 in v.
+__device__ __forceinline__ void quantize_sb(const float (&v)[8], int sb, int lane, uint8_t* xsl, float* sum32,
+                                            float* sum16, float* sxs) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+  uint32_t s0[2] = {0u, 0u}, s1[2] = {0u, 0u}, s2[2] = {0u, 0u};
+  float part = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    part += v[i];
+    const float q = v[i] * inv;
+    const float q0 = rintf(q);
+    const float u1 = (q - q0) * 254.0f;
+    const float q1 = rintf(u1);
+    const float q2 = rintf((u1 - q1) * 254.0f);
+    const int sh = 8 * (i & 3);
+    s0[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q0)) & 0xFFu) << sh;
+    s1[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q1)) & 0xFFu) << sh;
+    s2[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q2)) & 0xFFu) << sh;
+  }
+  // lane covers elements 8*lane .. +8: sub-block j = lane / 4, offset 8 * (lane % 4)
+  uint8_t* dst = xsl + (static_cast<size_t>(sb) * 8 + (lane >> 2)) * 96 + 8 * (lane & 3);
+  *reinterpret_cast<uint2*>(dst) = make_uint2(s0[0], s0[1]);
+  *reinterpret_cast<uint2*>(dst + 32) = make_uint2(s1[0], s1[1]);
+  *reinterpret_cast<uint2*>(dst + 64) = make_uint2(s2[0], s2[1]);
+  const float p16 = part + __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+  if ((lane & 1) == 0) sum16[sb * 16 + (lane >> 1)] = p16;
+  const float p32 = p16 + __shfl_xor_sync(0xFFFFFFFFu, p16, 2);
+  if ((lane & 3) == 0) sum32[sb * 8 + (lane >> 2)] = p32;
+  if (lane == 0) sxs[sb] = amax > 0.f ? amax / 127.0f : 0.f;
+}
+
+
 }  // namespace m3g

@@ -61,6 +61,11 @@ struct MmaArgs {
   int PRE;            // stages issued before the grid dependency resolves
   int tail_first;     // 1: a CTA's partial last row group is visited first
   int rows_per_cta;
+  // Non-null (plain GEMV of a host-buffer call): every CTA adds 1 to *fin_cnt
+  // when it is done, and the last one stores *status to *status_host (mapped
+  // host memory) and clears the count.
+  uint32_t* status_host;
+  unsigned int* fin_cnt;
   int off_xsl, off_sum32, off_sum16, off_scale, off_red, off_bar;
   // Fused input transform and epilogue (all zero for a plain GEMV):
   //   xmode 0: the GEMV input is x
@@ -196,6 +201,29 @@ cudaError_t launch_umma_q4k(const UmmaArgs& a, const float* x, long long in_dim,
                             size_t smem, cudaStream_t st, bool pdl);
 int umma_xtile(int nb);
 
+// Batch-1 Q4_K GEMV on tcgen05, kind::i8 (m3g_tc8.cu).  One CTA per SM owns
+// rows [blockIdx * rows_per_cta, ...), cut into tiles of tile_rows (<= 128)
+// rows; the weight tensor maps are built at launch from w.
+struct Tc8Args {
+  const float* x;      // x[in_dim], 16-byte aligned
+  float* y;            // y[rows]
+  uint32_t* status;    // error word of the call
+  uint32_t* status_host;  // non-null: the last CTA stores *status here (mapped host memory)
+  unsigned int* fin_cnt;  // CTAs done, for status_host (cleared by the last CTA)
+  long long rows;
+  int NSB, tile_rows, rows_per_cta, NSW, PRE;
+  int off_hdr, off_b, off_xsl, off_sum32, off_sum16, off_scale, off_bar;
+};
+struct Tc8Plan {
+  Tc8Args a{};
+  int grid = 0;
+  long long RB = 0;
+  size_t smem = 0;
+};
+bool plan_tc8(long long in_dim, long long rows, const uint8_t* w, const float* x, int sms, int smem_optin,
+              Tc8Plan& p);
+cudaError_t launch_tc8(const Tc8Plan& p, const uint8_t* w, cudaStream_t st, bool pdl);
+
 int mma_sb_bytes(int fmt);
 cudaError_t launch_gemv_mma(int fmt, const MmaArgs& a, int tps, int wk, int grid, size_t smem, cudaStream_t st,
                             bool pdl);
@@ -206,9 +234,8 @@ cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float
                                 long long nblocks, int grid, cudaStream_t st);
 cudaError_t launch_dequant(int fmt, const uint8_t* w, float* out, long long n_elems, int grid, cudaStream_t st);
 
-// Host-buffer GEMV I/O through mapped pinned memory (device-side aliases):
-// x in (n % 4 == 0, 16-byte aligned), and the status word out after the GEMV.
+// x of a host-buffer GEMV from mapped pinned host memory (device alias; n % 4
+// == 0, 16-byte aligned) into device memory.
 cudaError_t launch_host_x_in(const float* hx_dev, float* dx, long long n, cudaStream_t st);
-cudaError_t launch_host_status_out(const uint32_t* dstatus, uint32_t* hstatus_dev, cudaStream_t st, bool pdl);
 
 }  // namespace m3g

@@ -336,32 +336,11 @@ __global__ void __launch_bounds__(256) k_host_x_in(const float4* __restrict__ hx
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) dx[i] = hx[i];
 }
 
-// The call's kernel status word to mapped pinned host memory (a plain store,
-// after the GEMV before it has completed), so that the host reads it without
-// a device-to-host copy.
-__global__ void k_host_status_out(const uint32_t* __restrict__ dstatus, volatile uint32_t* hstatus) {
-  grid_dep_wait();
-  *hstatus = *dstatus;
-}
-
 cudaError_t launch_host_x_in(const float* hx_dev, float* dx, long long n, cudaStream_t st) {
   const int n4 = static_cast<int>(n / 4);
   const int grid = std::max(1, std::min(16, (n4 + 255) / 256));
   k_host_x_in<<<grid, 256, 0, st>>>(reinterpret_cast<const float4*>(hx_dev), reinterpret_cast<float4*>(dx), n4);
   return cudaGetLastError();
-}
-
-cudaError_t launch_host_status_out(const uint32_t* dstatus, uint32_t* hstatus_dev, cudaStream_t st, bool pdl) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
-  cfg.blockDim = dim3(1);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_host_status_out, dstatus, static_cast<volatile uint32_t*>(hstatus_dev));
 }
 
 cudaError_t launch_dequant(int fmt, const uint8_t* w, float* out, long long n_elems, int grid, cudaStream_t st) {

@@ -370,43 +370,6 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, long long row)
   return (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(row));
 }
 
-// x -> three int8 slices of super-block sb and its group sums; lane holds
-// elements 8*lane .. 8*lane+7 in v.
-__device__ __forceinline__ void quantize_sb(const float (&v)[8], int sb, int lane, uint8_t* xsl, float* sum32,
-                                            float* sum16, float* sxs) {
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-  const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-  uint32_t s0[2] = {0u, 0u}, s1[2] = {0u, 0u}, s2[2] = {0u, 0u};
-  float part = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    part += v[i];
-    const float q = v[i] * inv;
-    const float q0 = rintf(q);
-    const float u1 = (q - q0) * 254.0f;
-    const float q1 = rintf(u1);
-    const float q2 = rintf((u1 - q1) * 254.0f);
-    const int sh = 8 * (i & 3);
-    s0[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q0)) & 0xFFu) << sh;
-    s1[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q1)) & 0xFFu) << sh;
-    s2[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q2)) & 0xFFu) << sh;
-  }
-  // lane covers elements 8*lane .. +8: sub-block j = lane / 4, offset 8 * (lane % 4)
-  uint8_t* dst = xsl + (static_cast<size_t>(sb) * 8 + (lane >> 2)) * 96 + 8 * (lane & 3);
-  *reinterpret_cast<uint2*>(dst) = make_uint2(s0[0], s0[1]);
-  *reinterpret_cast<uint2*>(dst + 32) = make_uint2(s1[0], s1[1]);
-  *reinterpret_cast<uint2*>(dst + 64) = make_uint2(s2[0], s2[1]);
-  const float p16 = part + __shfl_xor_sync(0xFFFFFFFFu, part, 1);
-  if ((lane & 1) == 0) sum16[sb * 16 + (lane >> 1)] = p16;
-  const float p32 = p16 + __shfl_xor_sync(0xFFFFFFFFu, p16, 2);
-  if ((lane & 3) == 0) sum32[sb * 8 + (lane >> 2)] = p32;
-  if (lane == 0) sxs[sb] = amax > 0.f ? amax / 127.0f : 0.f;
-}
-
 // One CTA's arrival in a peer exchange (after its stores are fenced): the
 // CTA completing this step's count pushes the local greedy key to the peers
 // and signals each peer once.
@@ -426,6 +389,16 @@ __device__ __forceinline__ void peer_arrive(const MmaArgs& a) {
     __threadfence_system();
   }
   for (int p = 0; p < a.npeer; ++p) atomicAdd_system(a.peer_cnt[p], 1u);
+}
+
+// A CTA of a host-buffer call is done: the last one returns the status word
+// to the host (a plain store into mapped memory) and clears the count.
+__device__ __forceinline__ void host_status_count(const MmaArgs& a) {
+  __threadfence();
+  if (atomicAdd(a.fin_cnt, 1u) == gridDim.x - 1) {
+    *a.fin_cnt = 0u;
+    *reinterpret_cast<volatile uint32_t*>(a.status_host) = *reinterpret_cast<volatile uint32_t*>(a.status);
+  }
 }
 
 // Named barriers of the kernel (0 is __syncthreads): 1..WK pair the warps of
@@ -461,6 +434,8 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
         grid_dep_wait();
         peer_arrive(a);
       }
+    } else {
+      if (a.status_host && threadIdx.x == 0) host_status_count(a);
     }
     return;
   }
@@ -598,6 +573,12 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
       atomicOr(a.status, kStatusCopyTimeout);
       // Let copies still in flight land (bounded) before the CTA exits.
       for (int s = 0; s < a.NS; ++s) (void)mbar_wait_bounded(&full[s], 0u, kMmaTimeoutNs / 8);
+    }
+    if constexpr (!FUSED) {
+      if (a.status_host) {
+        __syncwarp();
+        if (lane == 0) host_status_count(a);
+      }
     }
     return;
   }

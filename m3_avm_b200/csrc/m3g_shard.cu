@@ -5,8 +5,8 @@
 // the local rows straight into this rank's slot of the gather buffer, and the
 // other ranks' slots arrive in one of two ways:
 //
-//  * peer stores (default when every rank can map every other rank's
-//    exchange region over NVLink): the GEMV's epilogue stores each row into
+//  * peer stores (tuning key shard_p2p, when every rank can map every other
+//    rank's exchange region over NVLink): the GEMV's epilogue stores each row into
 //    every peer's exchange region as well, and the CTA that completes the
 //    rank's rows adds 1 to every peer's arrival counter after a system-scope
 //    fence -- the all-gather is fused into the GEMV, tile by tile.  A small
@@ -14,7 +14,12 @@
 //    peers' slots into the caller's buffer.  The regions are double-buffered
 //    by call parity, so a rank one call ahead never overwrites rows a peer
 //    still copies;
-//  * otherwise one in-place NCCL all-gather of the fp32 slices.
+//  * otherwise (the default) one in-place NCCL all-gather of the fp32 slices.
+//
+// Measured on 2 B200s (Q4_K 14336 x 4096 per call): the local rows alone take
+// 6.0 us, with the NCCL all-gather 16.4 us, with peer stores 22.0 us (the
+// system-scope fences, the arrival atomics and the separate gather launch
+// cost more than NCCL's own kernel), so NCCL is the default.
 //
 // Communicator creation is non-blocking with a wall-clock limit: a rank that
 // never joins makes create() abort the communicator and return M3G_ETIMEOUT
