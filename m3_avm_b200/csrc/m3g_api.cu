@@ -101,7 +101,8 @@ struct Tuning {
   int64_t mma_tail_first = 1;     // tensor-core GEMV: a CTA's partial row group first
   int64_t offload_mapped = 1;     // batch-1 host-buffer calls: x, y, status through mapped pinned memory
   int64_t shard_p2p = 0;          // shard contexts: rows exchanged by peer stores from the GEMV epilogue (else NCCL)
-  int64_t tc8 = 0;                // batch-1 Q4_K GEMV on tcgen05 kind::i8 (k_tc8_q4k, K <= 4096); slower than mma.sync
+  int64_t tc8 = 0;                // batch-1 Q4_K GEMV on tcgen05 kind::i8 (k_tc8_q4k, K <= 4096)
+  int64_t tc8_pre = 0;            // k_tc8_q4k stages streamed before x is loaded (0: all)
 };
 Tuning g_tune;
 
@@ -324,6 +325,7 @@ int gemv_launch(const DevState& ds, const FmtInfo& f, const uint8_t* w, const fl
     tp.a.status = ds.status;
     tp.a.status_host = ds.status_host;
     tp.a.fin_cnt = ds.fin_cnt;
+    if (g_tune.tc8_pre > 0 && g_tune.tc8_pre < tp.a.PRE) tp.a.PRE = static_cast<int>(g_tune.tc8_pre);
     cudaError_t e = m3g::launch_tc8(tp, w, st, g_tune.pdl != 0);
     if (e != cudaSuccess) return cuda_fail(e, "k_tc8_q4k launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -750,6 +752,7 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "offload_mapped")) g_tune.offload_mapped = value != 0;
   else if (!strcmp(key, "shard_p2p")) g_tune.shard_p2p = value != 0;
   else if (!strcmp(key, "tc8")) g_tune.tc8 = value != 0;
+  else if (!strcmp(key, "tc8_pre") && value >= 0 && value <= 64) g_tune.tc8_pre = value;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));
   return M3G_OK;
 }

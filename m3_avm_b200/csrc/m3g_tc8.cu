@@ -20,35 +20,42 @@
 // Per CTA (one per SM): a contiguous range of rows, cut into tiles of at most
 // 128 rows (the MMA's M; a tile's TMA box is exactly its rows), every
 // super-block of each.  No tile is shared between CTAs, so no fix-up pass.
-// Units (tile, super-block) flow through NSW stages:
+// Units (tile, super-block) flow through kNST shared-memory stages and kNA
+// tensor-memory A buffers:
 //   producer  warp 0: one 2-D tensor copy of the unit's quants (128-byte
 //             rows, 128-byte swizzle) and one of its 16-byte block headers;
 //   maskers   warps 1-8, one row per thread: warps 1-4 copy the row's 128
 //             quant bytes into tensor memory as they are (the raw A operand),
-//             warps 5-8 masked with 0xF0 (the 16 hi operand), into the A
-//             buffer of the unit's stage;
-//   issuers   warps 13-14: two chunks each, two MMAs per chunk (A in tensor
-//             memory, B in shared memory; M = 128, N = 16, K = 32), one
-//             commit per unit;
-//   readout   warps 9-12, one row per thread: the four chunk accumulators
-//             back from tensor memory, scales, d, dmin, the sum over
-//             super-blocks, y.
-// Before the units, warps 1-12 turn x into int8 slices and lay out the x
-// operand tiles of every super-block once (shared memory, K <= 4096).
-// Each stage has its own A buffer, so the maskers wait only for the stage's
-// copy: the stage is refilled after the readout of the unit that last used
-// it, which follows that unit's MMAs.  Every wait is bounded; a timeout
-// raises the copy-timeout status bit and every role leaves its loop, so the
-// CTA frees its tensor memory and exits.
+//             warps 5-8 masked with 0xF0 (the 16 hi operand);
+//   readout   warps 9-12, one row per thread: the eight accumulators back
+//             from tensor memory, scales, d, dmin, the sum over super-blocks,
+//             y;
+//   issuers   warps 13-20: one MMA each per unit (chunk c = i / 2, raw or
+//             masked = i % 2; A in tensor memory, B in shared memory; M = 128,
+//             N = 16, K = 32) into its own accumulator, and one commit.  A
+//             kind::i8 MMA holds its issuing thread for ~230 SM clocks
+//             whatever N is, while eight issuing warps overlap almost fully
+//             (~35 clocks per MMA, measured on B200), so the eight MMAs of a
+//             unit go out from eight warps at once.
+// Before their first unit, the readout and issuer warps turn x into int8
+// slices written straight into the x operand tiles of every super-block
+// (K <= 4096); the maskers and the producer run ahead meanwhile.  With PRE <
+// kNST the producer streams only PRE stages until x is in registers, so the
+// loads of x do not queue behind the whole ring.  An x tile holds only the
+// eight rows of N that can be nonzero; the descriptor's row-group stride
+// points the other eight at a shared block of zeros.  Every wait is bounded;
+// a timeout raises the copy-timeout status bit and every role leaves its
+// loop, so the CTA frees its tensor memory and exits.
 //
-// Off by default (tuning key tc8): measured on B200, one kind::i8 MMA with
-// M = 128, K = 32 occupies the tensor core for ~200 SM clocks whatever N is
-// (16 to 256) and wherever A lies (tensor or shared memory), and a unit needs
-// eight of them, so the issuers bound a unit at ~560 ns.  The headline shape
-// (14336 x 4096, 97 rows and 16 units per SM) then takes 15.4 us against
-// 9.3 us for the mma.sync kernel: for one vector the tensor core's A intake
-// (4 KB per MMA, two passes over the quants) is below the HBM rate.  The
-// kernel stays as the tested tcgen05 formulation of the batch-1 product.
+// Off by default (tuning key tc8): on the headline shape (14336 x 4096, 97
+// rows and 16 units per SM) it takes 12.5 us against 9.3 us for the mma.sync
+// kernel.  A phase trace of one CTA shows the tensor-core side keeping up
+// (masker ~150 ns, issue ~250 ns, readout ~250 ns a unit, overlapped); what
+// binds is the weight stream: the row-strided boxes (one 128- and one
+// 16-byte piece per row and unit) land at ~30 GB/s per SM inside the kernel,
+// and x arrives ~2.5 us after the CTA starts.  A 3-D box of two super-blocks
+// per copy (144-byte rows) landed at ~20 GB/s per SM, with L2-resident
+// weights as well.
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
@@ -65,16 +72,20 @@ namespace {
 
 constexpr int kRawStage = 128 * 128;  // quants of one unit: up to 128 rows x 128 bytes
 constexpr int kHdrStage = 128 * 16;   // block headers of one unit: up to 128 rows x 16 bytes
-constexpr int kBTile = 4096;          // x operand of one super-block: 4 chunks x 2 K-steps x (16 rows x 32 bytes)
-constexpr int kNSW = 6;               // stages (one tensor-memory A buffer each)
+constexpr int kStage = kRawStage + kHdrStage;
+constexpr int kBTile = 2048;          // x operand of one super-block: [chunk 4][K-step 2][K half 2][row 8][16 bytes]
+constexpr int kZeroBytes = 256;       // the zero row group every x tile's rows 8-15 point at
+constexpr int kNST = 8;               // shared-memory stages
+constexpr int kNA = 4;                // tensor-memory A buffers
 constexpr int kMaxNSB = 16;           // super-blocks whose x tiles fit shared memory (K <= 4096)
-constexpr int kMaskWarps = 8, kReadWarps = 4, kIssuers = 2;
+constexpr int kMaskWarps = 8, kReadWarps = 4, kIssuers = 8;
 constexpr int kProducerW = 0, kMask0 = 1, kRead0 = kMask0 + kMaskWarps, kIssue0 = kRead0 + kReadWarps;
-constexpr int kThreads = 32 * (kIssue0 + kIssuers);  // 480
-// TMEM columns: A operands [kNSW][raw 32 | 16 hi 32] (4 int8 per column),
-// then accumulators [2][4 chunks][16].
-constexpr uint32_t kTmemA = 0, kTmemD = 64 * kNSW, kTmemCols = 512;
-static_assert(kTmemD + 128 <= kTmemCols, "TMEM columns");
+constexpr int kPrepWarps = kReadWarps + kIssuers;    // readout and issuers prepare x
+constexpr int kThreads = 32 * (kIssue0 + kIssuers);  // 672
+// TMEM columns: A operands [kNA][raw 32 | 16 hi 32] (4 int8 per column),
+// then accumulators [2][8 MMAs][16].
+constexpr uint32_t kTmemA = 0, kTmemD = 64 * kNA, kTmemCols = 512;
+static_assert(kTmemD + 2 * 16 * kIssuers <= kTmemCols, "TMEM columns");
 constexpr uint64_t kWaitNs = 2000000000ull;          // 2 s
 
 __device__ __forceinline__ void tc_alloc(uint32_t* slot, uint32_t ncols) {
@@ -157,6 +168,61 @@ __device__ __forceinline__ void tc8_status_count(const Tc8Args& a) {
   }
 }
 
+// x -> three int8 slices of super-block sb written into its x operand tile;
+// lane holds elements 8*lane .. 8*lane+7 in v (sub-block j = lane / 4, bytes
+// 8*(lane%4) .. of its 32).  Chunk c = j / 2 of the quants pairs lo quants
+// with sub-block 2c and hi quants with 2c + 1:
+//   K-step 0 (raw quants):    rows 0-2 = slices of 2c, rows 3-7 zero;
+//   K-step 1 (16 hi quants):  rows 0-2 = -slices of 2c, rows 3-5 = slices
+//                             of 2c + 1, rows 6-7 zero.
+// Also the sub-block sums of x (sum32) and the super-block scale (sxs).
+__device__ __forceinline__ void quantize_sb_tile(const float (&v)[8], int sb, int lane, uint8_t* bop, float* sum32,
+                                                 float* sxs) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+  uint32_t sl[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+  float part = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    part += v[i];
+    const float q = v[i] * inv;
+    const float q0 = rintf(q);
+    const float u1 = (q - q0) * 254.0f;
+    const float q1 = rintf(u1);
+    const float q2 = rintf((u1 - q1) * 254.0f);
+    const int sh = 8 * (i & 3);
+    sl[0][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q0)) & 0xFFu) << sh;
+    sl[1][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q1)) & 0xFFu) << sh;
+    sl[2][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(q2)) & 0xFFu) << sh;
+  }
+  const int j = lane >> 2, c = j >> 1, h = (lane >> 1) & 1;
+  uint8_t* t0 = bop + static_cast<size_t>(sb) * kBTile + c * 512 + h * 128 + 8 * (lane & 1);  // K-step 0, row 0
+  uint8_t* t1 = t0 + 256;                                                                      // K-step 1, row 0
+  const uint2 z = make_uint2(0u, 0u);
+  if ((j & 1) == 0) {
+#pragma unroll
+    for (int n = 0; n < 3; ++n) {
+      *reinterpret_cast<uint2*>(t0 + 16 * n) = make_uint2(sl[n][0], sl[n][1]);
+      *reinterpret_cast<uint2*>(t1 + 16 * n) = make_uint2(__vsub4(0u, sl[n][0]), __vsub4(0u, sl[n][1]));
+    }
+#pragma unroll
+    for (int n = 3; n < 8; ++n) *reinterpret_cast<uint2*>(t0 + 16 * n) = z;
+  } else {
+#pragma unroll
+    for (int n = 0; n < 3; ++n) *reinterpret_cast<uint2*>(t1 + 16 * (3 + n)) = make_uint2(sl[n][0], sl[n][1]);
+    *reinterpret_cast<uint2*>(t1 + 16 * 6) = z;
+    *reinterpret_cast<uint2*>(t1 + 16 * 7) = z;
+  }
+  float p32 = part + __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+  p32 += __shfl_xor_sync(0xFFFFFFFFu, p32, 2);
+  if ((lane & 3) == 0) sum32[sb * 8 + j] = p32;
+  if (lane == 0) sxs[sb] = amax > 0.f ? amax / 127.0f : 0.f;
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -172,31 +238,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   const int NSB = a.NSB, TR = a.tile_rows;
-  constexpr int NSW = kNSW;
   const int ntiles = static_cast<int>((row_end - row0 + TR - 1) / TR);
-  const int K = ntiles * NSB;  // units: (tile, super-block), tile-major
+  const int K = ntiles * NSB;      // units: (tile, super-block), tile-major
 
-  uint8_t* raw = smem;                       // [NSW][kRawStage], 1024-aligned
-  uint8_t* hdr = smem + a.off_hdr;           // [NSW][kHdrStage]
-  uint8_t* bop = smem + a.off_b;             // [NSB][kBTile]
-  uint8_t* xsl = smem + a.off_xsl;           // [NSB][8][3][32] int8
+  uint8_t* stg = smem;                       // [kNST][quants kRawStage | headers kHdrStage], 1024-aligned
+  uint8_t* bop = smem + a.off_b;             // [NSB][kBTile], then kZeroBytes of zeros
   float* sum32 = reinterpret_cast<float*>(smem + a.off_sum32);
-  float* sum16 = reinterpret_cast<float*>(smem + a.off_sum16);
   float* sxs = reinterpret_cast<float*>(smem + a.off_scale);
   uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + a.off_bar);
-  uint64_t* wempty = wfull + NSW;
-  uint64_t* afull = wempty + NSW;   // [NSW] A operands of the stage's unit in tensor memory (maskers)
-  uint64_t* dfree = afull + NSW;    // [2] accumulator buffer read back (readout)
+  uint64_t* wempty = wfull + kNST;
+  uint64_t* afull = wempty + kNST;  // [kNA] A operands of unit k in buffer k % kNA (maskers)
+  uint64_t* dfree = afull + kNA;    // [2] accumulator buffer read back (readout)
   uint64_t* sbdone = dfree + 2;     // [4] MMAs of unit k complete (one commit per issuer)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sbdone + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   if (tid == 0) {
-    for (int s = 0; s < NSW; ++s) {
+    for (int s = 0; s < kNST; ++s) {
       mbar_init(&wfull[s], 1);
       mbar_init(&wempty[s], kReadWarps);
-      mbar_init(&afull[s], kMaskWarps);
     }
+    for (int s = 0; s < kNA; ++s) mbar_init(&afull[s], kMaskWarps);
     for (int s = 0; s < 2; ++s) mbar_init(&dfree[s], kReadWarps);
     for (int s = 0; s < 4; ++s) mbar_init(&sbdone[s], kIssuers);
     *abort_flag = 0;
@@ -217,47 +279,85 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProducerW) {
     // ------------------------------------------------------------ producer
+    const uint64_t pol = l2_evict_first_policy();
+    const uint32_t tx = static_cast<uint32_t>(TR) * (128u + 16u);  // whole boxes, rows past the end included
+    auto issue = [&](int k) {
+      const int t = k / NSB, sb = k - t * NSB, ws = k % kNST;
+      const int y = static_cast<int>(row0 + static_cast<long long>(t) * TR);
+      uint8_t* dst = stg + static_cast<size_t>(ws) * kStage;
+      mbar_arrive_expect_tx(&wfull[ws], tx);
+      tma_2d(dst, &wq, sb * 144 + 16, y, &wfull[ws], pol);
+      tma_2d(dst + kRawStage, &wh, sb * 144, y, &wfull[ws], pol);
+    };
+    // Weights are never written by an earlier kernel: the first PRE stages
+    // stream before the grid dependency resolves, the rest once x is loaded.
+    const int pre = min(min(a.PRE, kNST), K);
+    if (lane == 0)
+      for (int g = 0; g < pre; ++g) issue(g);
+    grid_dep_wait();
+    grid_dep_launch();
+    if (a.PRE < kNST) named_bar_sync(2, 32 * (kPrepWarps + 1));
     if (lane == 0) {
-      const uint64_t pol = l2_evict_first_policy();
-      const uint32_t tx = static_cast<uint32_t>(TR) * (128u + 16u);
-      auto issue = [&](int k) {
-        const int t = k / NSB, s = k - t * NSB, ws = k % NSW;
-        const int y = static_cast<int>(row0 + static_cast<long long>(t) * TR);
-        mbar_arrive_expect_tx(&wfull[ws], tx);
-        tma_2d(raw + static_cast<size_t>(ws) * kRawStage, &wq, s * 144 + 16, y, &wfull[ws], pol);
-        tma_2d(hdr + static_cast<size_t>(ws) * kHdrStage, &wh, s * 144, y, &wfull[ws], pol);
-      };
-      // Weights are never written by an earlier kernel: the first stages
-      // stream before the grid dependency resolves.
-      const int pre = min(NSW, K);
-      for (int k = 0; k < pre; ++k) issue(k);
-      grid_dep_wait();
-      grid_dep_launch();
       int issued = pre;
-      for (int k = NSW; k < K; ++k) {
-        const int ws = k % NSW;
-        if (!mbar_wait_bounded(&wempty[ws], ((k / NSW) & 1) ^ 1, kWaitNs, abort_flag)) {
+      for (int g = pre; g < K; ++g) {
+        const int ws = g % kNST;
+        if (g >= kNST && !mbar_wait_bounded(&wempty[ws], ((g / kNST) & 1) ^ 1, kWaitNs, abort_flag)) {
           fail();
           break;
         }
-        issue(k);
-        issued = k + 1;
+        issue(g);
+        issued = g + 1;
       }
       // every copy issued lands before the CTA can exit
-      for (int k = max(0, issued - NSW); k < issued; ++k)
-        (void)mbar_wait_bounded(&wfull[k % NSW], (k / NSW) & 1, kWaitNs / 8, nullptr);
+      for (int g = max(0, issued - kNST); g < issued; ++g)
+        (void)mbar_wait_bounded(&wfull[g % kNST], (g / kNST) & 1, kWaitNs / 8, nullptr);
     }
     __syncwarp();
-  } else if (warp < kIssue0) {
-    // ------------------------------------------------------------ x slices and x tiles (warps 1-12)
+  } else if (warp < kRead0) {
+    // ------------------------------------------------------------ maskers
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = 32 * q + lane;
+    const uint32_t tl = tbase + (static_cast<uint32_t>(32 * q) << 16);
+    const bool masked = warp - kMask0 >= 4;  // warps 5-8: the 16 hi operand
+    for (int k = 0; k < K && !*abort_flag; ++k) {
+      const int g = k, ws = g % kNST, ab = k % kNA;
+      // the stage's quants have landed; the A buffer's previous unit
+      // (k - kNA) has finished its MMAs
+      bool ok = mbar_wait_bounded(&wfull[ws], (g / kNST) & 1, kWaitNs, abort_flag);
+      if (ok && k >= kNA) ok = mbar_wait_bounded(&sbdone[k & 3], ((k >> 2) & 1) ^ 1, kWaitNs, abort_flag);
+      if (!__all_sync(0xFFFFFFFFu, ok)) {
+        if (lane == 0) fail();
+        break;
+      }
+      // row r's 128 quant bytes in natural order: 16-byte chunk j of a
+      // 128-byte-swizzled row lies at chunk j ^ (r % 8)
+      const uint8_t* rowp = stg + static_cast<size_t>(ws) * kStage + r * 128;
+      uint32_t w[32];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint4 c4 = *reinterpret_cast<const uint4*>(rowp + ((j ^ (r & 7)) << 4));
+        w[4 * j] = c4.x; w[4 * j + 1] = c4.y; w[4 * j + 2] = c4.z; w[4 * j + 3] = c4.w;
+      }
+      if (masked) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] &= 0xF0F0F0F0u;
+      }
+      tc_fence_after();
+      tc_st32(tl + kTmemA + static_cast<uint32_t>(ab * 64 + (masked ? 32 : 0)), w);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[ab]);
+    }
+  } else {
+    // ------------------------------------------------------------ x tiles (readout and issuer warps)
     grid_dep_wait();
     {
-      constexpr int kPrep = kMaskWarps + kReadWarps;
-      const int pw = warp - kMask0;
+      const int pw = warp - kRead0;
       float v[2][8];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {  // NSB <= 16 < 2 * kPrep: every load in flight at once
-        const int sb = pw + kPrep * u;
+      for (int u = 0; u < 2; ++u) {  // NSB <= 16 < 2 * kPrepWarps: every load in flight at once
+        const int sb = pw + kPrepWarps * u;
         if (sb < NSB) {
           const float4* xp = reinterpret_cast<const float4*>(a.x + 256 * sb + 8 * lane);
           const float4 v0 = __ldg(xp), v1 = __ldg(xp + 1);
@@ -265,80 +365,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           v[u][4] = v1.x; v[u][5] = v1.y; v[u][6] = v1.z; v[u][7] = v1.w;
         }
       }
+      if (a.PRE < kNST) {  // x is in registers: the producer may fill the ring
+        float t = 0.f;
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          if (pw + kPrepWarps * u < NSB) t += v[u][0];
+        asm volatile("" ::"f"(t));
+        named_bar_arrive(2, 32 * (kPrepWarps + 1));
+      }
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
-        const int sb = pw + kPrep * u;
-        if (sb < NSB) quantize_sb(v[u], sb, lane, xsl, sum32, sum16, sxs);
+        const int sb = pw + kPrepWarps * u;
+        if (sb < NSB) quantize_sb_tile(v[u], sb, lane, bop, sum32, sxs);
       }
-    }
-    named_bar_sync(1, 32 * (kMaskWarps + kReadWarps));
-    // x tiles of every super-block, 16-byte pieces of K-major core matrices
-    // (8 rows x 16 bytes; the two K halves 128 bytes apart, row groups 256):
-    // chunk c, K-step 0 rows 0-2 = x_lo slices (against the raw quants),
-    // K-step 1 rows 0-2 = -x_lo and rows 3-5 = x_hi slices (against 16 hi);
-    // every other row zero.
-    for (int pc = tid - 32 * kMask0; pc < NSB * (kBTile / 16); pc += 32 * (kMaskWarps + kReadWarps)) {
-      const int sb = pc / (kBTile / 16), off = (pc % (kBTile / 16)) * 16;
-      const int c = off / 1024, ks = (off % 1024) / 512, rg = (off % 512) / 256, h = (off % 256) / 128;
-      const int n = rg * 8 + (off % 128) / 16;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      const bool lo = n < 3, hi = ks == 1 && n >= 3 && n < 6;
-      if (lo || hi) {
-        const int j = hi ? 2 * c + 1 : 2 * c, sl = hi ? n - 3 : n;
-        v = *reinterpret_cast<const uint4*>(xsl + (static_cast<size_t>(sb) * 8 + j) * 96 + sl * 32 + 16 * h);
-        if (ks == 1 && lo) v = make_uint4(__vsub4(0u, v.x), __vsub4(0u, v.y), __vsub4(0u, v.z), __vsub4(0u, v.w));
-      }
-      *reinterpret_cast<uint4*>(bop + static_cast<size_t>(pc) * 16) = v;
+      if (pw == 0)
+        *reinterpret_cast<uint2*>(bop + static_cast<size_t>(NSB) * kBTile + 8 * lane) = make_uint2(0u, 0u);
     }
     fence_proxy_async_smem();
-    named_bar_sync(1, 32 * (kMaskWarps + kReadWarps));
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int r = 32 * q + lane;
-    const uint32_t tl = tbase + (static_cast<uint32_t>(32 * q) << 16);
-    if (warp < kRead0) {
-      // ---------------------------------------------------------- maskers
-      const bool masked = warp - kMask0 >= 4;  // warps 5-8: the 16 hi operand
+    named_bar_sync(1, 32 * kPrepWarps);
+    if (warp < kIssue0) {
+      // ---------------------------------------------------------- readout
+      const int q = warp & 3;
+      const int r = 32 * q + lane;
+      const uint32_t tl = tbase + (static_cast<uint32_t>(32 * q) << 16);
+      float acc = 0.f;
       for (int k = 0; k < K && !*abort_flag; ++k) {
-        const int ws = k % NSW;
-        const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(&wfull[ws], (k / NSW) & 1, kWaitNs, abort_flag));
-        if (!ok) {
+        const int ws = k % kNST, db = k & 1;
+        const int t = k / NSB, s = k - t * NSB;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&sbdone[k & 3], (k >> 2) & 1, kWaitNs, abort_flag))) {
           if (lane == 0) fail();
           break;
         }
-        // row r's 128 quant bytes in natural order: 16-byte chunk j of a
-        // 128-byte-swizzled row lies at chunk j ^ (r % 8)
-        const uint8_t* rowp = raw + static_cast<size_t>(ws) * kRawStage + r * 128;
-        uint32_t w[32];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint4 c4 = *reinterpret_cast<const uint4*>(rowp + ((j ^ (r & 7)) << 4));
-          w[4 * j] = c4.x; w[4 * j + 1] = c4.y; w[4 * j + 2] = c4.z; w[4 * j + 3] = c4.w;
-        }
-        if (masked) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) w[i] &= 0xF0F0F0F0u;
-        }
         tc_fence_after();
-        tc_st32(tl + kTmemA + static_cast<uint32_t>(ws * 64 + (masked ? 32 : 0)), w);
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[ws]);
-      }
-    } else {
-      // ---------------------------------------------------------- readout
-      float acc = 0.f;
-      for (int k = 0; k < K && !*abort_flag; ++k) {
-        const int ws = k % NSW, db = k & 1;
-        const int t = k / NSB, s = k - t * NSB;
-        if (!mbar_wait_bounded(&sbdone[k & 3], (k >> 2) & 1, kWaitNs, abort_flag)) {
-          fail();
-          break;
-        }
-        tc_fence_after();
-        const uint4 h = *reinterpret_cast<const uint4*>(hdr + static_cast<size_t>(ws) * kHdrStage + r * 16);
-        uint32_t v[32];
-        tc_ld4x8(tl + kTmemD + static_cast<uint32_t>(db * 64), v);
+        const uint4 h = *reinterpret_cast<const uint4*>(stg + static_cast<size_t>(ws) * kStage + kRawStage + r * 16);
+        uint32_t v[64];  // accumulator m = 2c + (0 raw, 1 masked), columns 0-7
+        const uint32_t d0 = tl + kTmemD + static_cast<uint32_t>(db * 16 * kIssuers);
+        tc_ld4x8(d0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tc_ld4x8(d0 + 64u, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -357,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int sb = static_cast<int>((sw >> (16 * (c & 1) + 8)) & 0xFFu);   // sub-block 2c + 1
 #pragma unroll
           for (int n = 0; n < 3; ++n) {
-            alo[n] += sa * static_cast<int>(v[8 * c + n]);
-            ahi[n] += sb * static_cast<int>(v[8 * c + 3 + n]);
+            alo[n] += sa * (static_cast<int>(v[16 * c + n]) + static_cast<int>(v[16 * c + 8 + n]));
+            ahi[n] += sb * static_cast<int>(v[16 * c + 8 + 3 + n]);
           }
         }
         const float main = static_cast<float>(16 * alo[0] + ahi[0]) +
@@ -379,32 +442,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc = 0.f;
         }
       }
-    }
-  } else {
-    // ------------------------------------------------------------ MMA issuers
-    const int ci = warp - kIssue0;
-    if (lane == 0) {
+    } else if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuers
+      const int i = warp - kIssue0, c = i >> 1, part = i & 1;  // part 0: raw quants, 1: 16 hi
       constexpr uint32_t idesc = idesc_i8_m128(16);
       const uint32_t b_a = smem_addr(bop);
+      const uint32_t z_a = b_a + static_cast<uint32_t>(NSB * kBTile);
       int last = -1;
       for (int k = 0; k < K; ++k) {
         if (*abort_flag) break;
-        const int ws = k % NSW, db = k & 1, s = k % NSB;
-        if (!mbar_wait_bounded(&afull[ws], (k / NSW) & 1, kWaitNs, abort_flag) ||
+        const int ab = k % kNA, db = k & 1, s = k % NSB;
+        if (!mbar_wait_bounded(&afull[ab], (k / kNA) & 1, kWaitNs, abort_flag) ||
             !mbar_wait_bounded(&dfree[db], ((k >> 1) & 1) ^ 1, kWaitNs, abort_flag)) {
           fail();
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = 2 * ci + cc;
-          const uint32_t d = tbase + kTmemD + static_cast<uint32_t>(db * 64 + c * 16);
-          const uint32_t at = tbase + kTmemA + static_cast<uint32_t>(ws * 64 + 8 * c);
-          const uint32_t bt = b_a + static_cast<uint32_t>(s * kBTile + c * 1024);
-          tc_mma_i8_ts(d, at, desc_plain(bt, 128u, 256u), idesc, 0u);
-          tc_mma_i8_ts(d, at + 32u, desc_plain(bt + 512u, 128u, 256u), idesc, 1u);
-        }
+        const uint32_t d = tbase + kTmemD + static_cast<uint32_t>(db * 16 * kIssuers + 16 * i);
+        const uint32_t at = tbase + kTmemA + static_cast<uint32_t>(ab * 64 + 32 * part + 8 * c);
+        const uint32_t bt = b_a + static_cast<uint32_t>(s * kBTile + c * 512 + part * 256);
+        tc_mma_i8_ts(d, at, desc_plain(bt, 128u, z_a - bt), idesc, 0u);
         tc_commit(&sbdone[k & 3]);
         last = k;
       }
@@ -446,31 +503,28 @@ bool plan_tc8(long long in_dim, long long rows, const uint8_t* w, const float* x
   const long long rpc = (rows + sms - 1) / sms;
   const long long ntiles = (rpc + 127) / 128;
   const long long tr = (rpc + ntiles - 1) / ntiles;
-  // shared memory: quant stages (1024-aligned for the 128-byte swizzle) |
-  // header stages | x tiles | x slices and sums | barriers
-  long long off = static_cast<long long>(kNSW) * kRawStage;
-  p.a.off_hdr = static_cast<int>(off);
-  off += static_cast<long long>(kNSW) * kHdrStage;
+  // shared memory: weight stages (1024-aligned for the 128-byte swizzle) |
+  // x tiles and the zero block | x sums and scales | barriers
+  long long off = static_cast<long long>(kNST) * kStage;
+  p.a.off_hdr = 0;
   p.a.off_b = static_cast<int>(off);
-  off += NSB * kBTile;
-  p.a.off_xsl = static_cast<int>(off);
-  off += (NSB * 768 + 127) / 128 * 128;
+  off += NSB * kBTile + kZeroBytes;
+  p.a.off_xsl = 0;
+  p.a.off_sum16 = 0;
   p.a.off_sum32 = static_cast<int>(off);
   off += NSB * 32;
-  p.a.off_sum16 = static_cast<int>(off);
-  off += NSB * 64;
   p.a.off_scale = static_cast<int>(off);
   off += (NSB * 4 + 15) / 16 * 16;
   p.a.off_bar = static_cast<int>(off);
-  off += (3 * kNSW + 6) * 8 + 16;
+  off += (2 * kNST + kNA + 6) * 8 + 16;
   p.smem = static_cast<size_t>(off + 1024);  // room to align the base to 1024 bytes
   if (static_cast<long long>(p.smem) > smem_optin) return false;
   p.a.rows = rows;
   p.a.NSB = static_cast<int>(NSB);
   p.a.tile_rows = static_cast<int>(tr);
   p.a.rows_per_cta = static_cast<int>(rpc);
-  p.a.NSW = kNSW;
-  p.a.PRE = kNSW;
+  p.a.NSW = kNST;
+  p.a.PRE = kNST;  // the caller may lower it (x first)
   p.grid = static_cast<int>((rows + rpc - 1) / rpc);
   p.RB = NSB * 144;
   return true;
@@ -479,6 +533,7 @@ bool plan_tc8(long long in_dim, long long rows, const uint8_t* w, const float* x
 cudaError_t launch_tc8(const Tc8Plan& p, const uint8_t* w, cudaStream_t st, bool pdl) {
   auto encode = tc8_encoder();
   if (!encode) return cudaErrorNotSupported;
+  // quants: box 128 bytes x rows, 128-byte swizzle; headers: box 16 bytes x rows
   CUtensorMap wq, wh;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.RB), static_cast<cuuint64_t>(p.a.rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.RB)};
