@@ -1117,10 +1117,17 @@ def main() -> int:
                          "batched: one Q4_K 28672x8192 GEMM; cpu-table: the reference CPU path of every "
                          "single-GEMV config on this host")
     ap.add_argument("--batch", type=int, default=8, help="columns of X for --workload batched")
+    ap.add_argument("--tune", action="append", default=[], metavar="KEY=VALUE",
+                    help="m3g_set_tuning(KEY, VALUE) before the run (repeatable), e.g. --tune tc8=1")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    for kv in args.tune:
+        from m3_avm_b200 import matvec_quant as MQ
+
+        key, _, val = kv.partition("=")
+        MQ.set_tuning(key, int(val))
     if args.workload == "cpu-table":
         return run_cpu_table(args)
     if args.workload == "decode":
