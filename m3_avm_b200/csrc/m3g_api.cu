@@ -5,6 +5,7 @@
 // m3g_kernels.cu.  There is no CPU fallback: without a device every compute
 // entry point returns M3G_ECUDA.
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -1026,8 +1027,9 @@ struct m3g_offload {
   float* hm_x_dev = nullptr;
   float* hm_y = nullptr;
   float* hm_y_dev = nullptr;
-  uint32_t* hm_st = nullptr;
+  uint32_t* hm_st = nullptr;      // [status, sequence number of the last call done]
   uint32_t* hm_st_dev = nullptr;
+  uint32_t host_seq = 0;          // sequence number of the last mapped call (device copy at d_out + 8)
   uint64_t calls = 0;
   std::unordered_map<uint64_t, ResidentTensor> tensors;
   // Host-buffer calls: one captured graph per tensor (copy x in, GEMV, copy y
@@ -1065,6 +1067,7 @@ void drop_graphs(m3g_offload* c) {
 }
 
 void free_io(m3g_offload* c) {
+  if (c->stream) cudaStreamSynchronize(c->stream);  // mapped calls return before their kernels exit
   drop_graphs(c);
   if (c->d_x) cudaFree(c->d_x);
   if (c->d_out) cudaFree(c->d_out);
@@ -1094,7 +1097,7 @@ int ensure_mapped(m3g_offload* c) {
   M3G_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->hm_x_dev), c->hm_x, 0));
   M3G_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->hm_y_dev), c->hm_y, 0));
   M3G_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->hm_st_dev), c->hm_st, 0));
-  *c->hm_st = 0u;
+  c->hm_st[0] = c->hm_st[1] = 0u;
   return M3G_OK;
 }
 
@@ -1106,6 +1109,10 @@ int ensure_io(m3g_offload* c, uint64_t batch) {
   M3G_CUDA(cudaMalloc(&c->d_x, nx * sizeof(float)));
   M3G_CUDA(cudaMalloc(&c->d_out, 16 + ny * sizeof(float)));
   M3G_CUDA(cudaMemset(c->d_out, 0, 16));
+  // The device's sequence word at d_out + 8 starts again at 0, and so do the
+  // host's count and the mapped copy (no kernel is in flight: free_io synced).
+  c->host_seq = 0;
+  if (c->hm_st) c->hm_st[1] = 0u;
   M3G_CUDA(cudaMallocHost(&c->h_x, nx * sizeof(float)));
   M3G_CUDA(cudaMallocHost(&c->h_out, 16 + ny * sizeof(float)));
   c->d_status = reinterpret_cast<uint32_t*>(c->d_out);
@@ -1327,7 +1334,28 @@ int m3g_offload_matvec_batch(m3g_offload* c, uint64_t tidx, const float* x, uint
   } else if (int rc = enqueue()) {
     return rc;
   }
-  M3G_CUDA(cudaStreamSynchronize(c->stream));
+  if (mapped) {
+    // The GEMV's last CTA publishes this call's sequence number after y and
+    // the status word (system-scope fences); wait for it on the host, bounded,
+    // instead of synchronising the stream.  On time-out fall back to the sync,
+    // which also surfaces a launch error.
+    const uint32_t want = c->host_seq + 1u;
+    volatile uint32_t* seq = c->hm_st + 1;
+    bool seen = *seq == want;
+    if (!seen) {
+      const auto t0 = std::chrono::steady_clock::now();
+      for (uint32_t it = 1; !(seen = *seq == want); ++it)
+        if ((it & 1023u) == 0u && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(2)) break;
+    }
+    if (!seen) {
+      M3G_CUDA(cudaStreamSynchronize(c->stream));
+      seen = *seq == want;
+    }
+    if (!seen) return fail(M3G_ECUDA, "host-buffer GEMV did not report completion");
+    c->host_seq = want;
+  } else {
+    M3G_CUDA(cudaStreamSynchronize(c->stream));
+  }
   memcpy(y, mapped ? c->hm_y : c->h_y, by);
   const uint32_t bits = mapped ? *static_cast<volatile uint32_t*>(c->hm_st) : *c->h_status;
   if (bits) {

@@ -61,9 +61,10 @@ struct MmaArgs {
   int PRE;            // stages issued before the grid dependency resolves
   int tail_first;     // 1: a CTA's partial last row group is visited first
   int rows_per_cta;
-  // Non-null (plain GEMV of a host-buffer call): every CTA adds 1 to *fin_cnt
-  // when it is done, and the last one stores *status to *status_host (mapped
-  // host memory) and clears the count.
+  // Non-null (plain GEMV of a host-buffer call): every CTA adds 1 to fin_cnt[0]
+  // when it is done, and the last one stores *status to status_host[0] (mapped
+  // host memory), clears the count and stores the call's sequence number
+  // fin_cnt[1] + 1 (kept in fin_cnt[1]) to status_host[1].
   uint32_t* status_host;
   unsigned int* fin_cnt;
   int off_xsl, off_sum32, off_sum16, off_scale, off_red, off_bar;
@@ -208,8 +209,8 @@ struct Tc8Args {
   const float* x;      // x[in_dim], 16-byte aligned
   float* y;            // y[rows]
   uint32_t* status;    // error word of the call
-  uint32_t* status_host;  // non-null: the last CTA stores *status here (mapped host memory)
-  unsigned int* fin_cnt;  // CTAs done, for status_host (cleared by the last CTA)
+  uint32_t* status_host;  // non-null: the last CTA stores [*status, sequence] here (mapped host memory)
+  unsigned int* fin_cnt;  // [CTAs done (cleared by the last CTA), sequence of the last call]
   long long rows;
   int NSB, tile_rows, rows_per_cta, NSW, PRE;
   int off_hdr, off_b, off_xsl, off_sum32, off_sum16, off_scale, off_bar;

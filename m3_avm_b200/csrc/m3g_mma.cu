@@ -391,13 +391,20 @@ __device__ __forceinline__ void peer_arrive(const MmaArgs& a) {
   for (int p = 0; p < a.npeer; ++p) atomicAdd_system(a.peer_cnt[p], 1u);
 }
 
-// A CTA of a host-buffer call is done: the last one returns the status word
-// to the host (a plain store into mapped memory) and clears the count.
+// A CTA of a host-buffer call is done: its rows of y (mapped host memory)
+// are made visible system-wide before it counts; the last CTA returns the
+// status word and then the call's sequence number (fin_cnt[1] + 1) to the
+// host, which waits for that number instead of synchronising the stream.
 __device__ __forceinline__ void host_status_count(const MmaArgs& a) {
-  __threadfence();
+  __threadfence_system();
   if (atomicAdd(a.fin_cnt, 1u) == gridDim.x - 1) {
     *a.fin_cnt = 0u;
-    *reinterpret_cast<volatile uint32_t*>(a.status_host) = *reinterpret_cast<volatile uint32_t*>(a.status);
+    volatile uint32_t* hs = a.status_host;
+    hs[0] = *reinterpret_cast<volatile uint32_t*>(a.status);
+    const uint32_t seq = a.fin_cnt[1] + 1u;
+    a.fin_cnt[1] = seq;
+    __threadfence_system();
+    hs[1] = seq;
   }
 }
 

@@ -160,11 +160,19 @@ __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x,
       : "memory");
 }
 
+// As host_status_count of the mma.sync GEMV: y visible system-wide before
+// the count; the last CTA returns the status word, then the call's sequence
+// number.
 __device__ __forceinline__ void tc8_status_count(const Tc8Args& a) {
-  __threadfence();
+  __threadfence_system();
   if (atomicAdd(a.fin_cnt, 1u) == gridDim.x - 1) {
     *a.fin_cnt = 0u;
-    *reinterpret_cast<volatile uint32_t*>(a.status_host) = *reinterpret_cast<volatile uint32_t*>(a.status);
+    volatile uint32_t* hs = a.status_host;
+    hs[0] = *reinterpret_cast<volatile uint32_t*>(a.status);
+    const uint32_t seq = a.fin_cnt[1] + 1u;
+    a.fin_cnt[1] = seq;
+    __threadfence_system();
+    hs[1] = seq;
   }
 }
 

@@ -426,3 +426,33 @@ def test_offload_mapped_and_copy_paths_agree(m3):
     assert np.array_equal(ys[0].view(np.uint32), ys[1].view(np.uint32))
     assert m3.matvec_quant.device_status(0) == 0
     g.close()
+
+
+def test_offload_mapped_calls_across_batches_and_tensors(m3):
+    """A mapped batch-1 call returns once its GEMV has published the call's
+    sequence number, without synchronising the stream.  Interleave tensors,
+    batch-1 calls (mapped), a batched call that regrows the staging buffers
+    (restarting the sequence) and the tc8 kernel; every result must match the
+    oracle and every call must return."""
+    g = m3.inference_gpu.GpuOffload.try_new(4096, 4096)
+    assert g is not None
+    raws = {t: m3.synth.weights(12, 4096, 1000 + 700 * t, seed=80 + t) for t in (1, 2)}
+    for t, r in raws.items():
+        assert g.upload(t, 12, r, 4096, 1000 + 700 * t)
+    xs = [m3.synth.activations(4096, seed=90 + i) for i in range(3)]
+    plan = [(1, 1, 0), (2, 1, 0), (1, 1, 0), (2, 3, 0), (1, 1, 0), (2, 1, 1), (1, 1, 1), (2, 1, 0)]
+    for t, batch, tc8 in plan:
+        out = 1000 + 700 * t
+        m3.matvec_quant.set_tuning("tc8", tc8)
+        try:
+            if batch == 1:
+                check_gemv(g.matvec(t, xs[0], 4096, out), raws[t], 12, 4096, out, xs[0])
+            else:
+                Y = g.matvec_batch(t, np.stack(xs[:batch]), 4096, out)
+                assert Y is not None
+                for b in range(batch):
+                    check_gemv(Y[b], raws[t], 12, 4096, out, xs[b])
+        finally:
+            m3.matvec_quant.set_tuning("tc8", 0)
+    assert m3.matvec_quant.device_status(0) == 0
+    g.close()
