@@ -617,16 +617,48 @@ __global__ void __launch_bounds__(32 * (WK * TPS + 1), 1) k_gemv_mma(const MmaAr
     // warp prepares exactly the super-blocks it consumes (its share [j0, j1) of
     // every k-chunk), so it never waits for another warp; with two tiles per
     // stage the warp of tile 0 prepares and its tile-1 partner waits for it.
-    if (ti == 0) {
-      for (int kcp = 0; kcp < a.NKC; ++kcp) {
-        const int sb0p = kcp * a.KC;
-        const int nsbp = min(a.KC, a.NSB - sb0p);
-        for (int sb = sb0p + wk * nsbp / WK; sb < sb0p + (wk + 1) * nsbp / WK; ++sb) {
-          const float4* xp4 = reinterpret_cast<const float4*>(a.x + 256 * sb + 8 * lane);
-          const float4 v0 = __ldg(xp4), v1 = __ldg(xp4 + 1);
-          const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-          quantize_sb(v, sb, lane, xsl, sum32, sum16, sxs);
+    // The loads of up to kXBatch super-blocks go out together, so a warp
+    // with several (long rows: one per k-chunk) pays one L2 round trip per
+    // batch instead of one per super-block.
+    if (ti == 0 && a.NKC == 1) {  // one k-chunk: at most 16 / WK super-blocks, loaded one by one
+      for (int sb = wk * a.NSB / WK; sb < (wk + 1) * a.NSB / WK; ++sb) {
+        const float4* xp4 = reinterpret_cast<const float4*>(a.x + 256 * sb + 8 * lane);
+        const float4 v0 = __ldg(xp4), v1 = __ldg(xp4 + 1);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        quantize_sb(v, sb, lane, xsl, sum32, sum16, sxs);
+      }
+    } else if (ti == 0) {
+      constexpr int kXBatch = 4;
+      int kcp = 0, sb = -1, sb_end = -1;  // the walk: [sb, sb_end) of k-chunk kcp
+      auto advance = [&]() {
+        while (sb >= sb_end && kcp < a.NKC) {
+          const int sb0p = kcp * a.KC, nsbp = min(a.KC, a.NSB - sb0p);
+          sb = sb0p + wk * nsbp / WK;
+          sb_end = sb0p + (wk + 1) * nsbp / WK;
+          ++kcp;
         }
+      };
+      advance();
+      while (sb < sb_end) {
+        float v[kXBatch][8];
+        int sbs[kXBatch];
+        int n = 0;
+#pragma unroll
+        for (int i = 0; i < kXBatch; ++i) {
+          if (sb < sb_end) {
+            const float4* xp4 = reinterpret_cast<const float4*>(a.x + 256 * sb + 8 * lane);
+            const float4 v0 = __ldg(xp4), v1 = __ldg(xp4 + 1);
+            v[i][0] = v0.x; v[i][1] = v0.y; v[i][2] = v0.z; v[i][3] = v0.w;
+            v[i][4] = v1.x; v[i][5] = v1.y; v[i][6] = v1.z; v[i][7] = v1.w;
+            sbs[i] = sb;
+            n = i + 1;
+            ++sb;
+            advance();
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kXBatch; ++i)
+          if (i < n) quantize_sb(v[i], sbs[i], lane, xsl, sum32, sum16, sxs);
       }
     }
   } else {
