@@ -142,6 +142,9 @@ struct m3g_shard {
   float* d_x = nullptr;    // [batch][max_in]
   float* d_ws = nullptr;   // gather buffer [world][batch][RPR]
   uint64_t cap_x = 0, cap_ws = 0;
+  float* h_x = nullptr;    // pinned staging of the host-buffer call: x
+  float* h_ws = nullptr;   // and the gathered y, [world][batch][RPR]
+  uint64_t cap_hx = 0, cap_hws = 0;
   uint64_t calls = 0;
   double timeout_s = 60.0;
   // Peer-store exchange: this rank's region (counters, then two halves of
@@ -294,6 +297,18 @@ int grow(float** p, uint64_t* cap, uint64_t n) {
   return M3G_OK;
 }
 
+// Pinned host staging, grown on demand: the copies are then one DMA each.
+int grow_pinned(float** p, uint64_t* cap, uint64_t n) {
+  if (n <= *cap) return M3G_OK;
+  if (*p) cudaFreeHost(*p);
+  *p = nullptr;
+  *cap = 0;
+  cudaError_t e = cudaMallocHost(p, n * sizeof(float));
+  if (e != cudaSuccess) return m3g::host_fail(M3G_ENOMEM, "shard staging: %s", cudaGetErrorString(e));
+  *cap = n;
+  return M3G_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -405,6 +420,8 @@ void m3g_shard_destroy(m3g_shard* c) {
   for (auto& kv : c->tensors) cudaFree(kv.second.d_raw);
   if (c->d_x) cudaFree(c->d_x);
   if (c->d_ws) cudaFree(c->d_ws);
+  if (c->h_x) cudaFreeHost(c->h_x);
+  if (c->h_ws) cudaFreeHost(c->h_ws);
   if (c->comm) {
     ncclResult_t r = ncclCommFinalize(c->comm);
     if (nccl_settle(c->comm, r, "ncclCommFinalize", c->timeout_s) == M3G_OK) ncclCommDestroy(c->comm);
@@ -531,21 +548,26 @@ int m3g_shard_matvec(m3g_shard* c, uint64_t tidx, const float* x, uint64_t batch
   const uint64_t ws = static_cast<uint64_t>(c->world) * batch * t.rpr;
   if (int rc = grow(&c->d_x, &c->cap_x, batch * in_dim)) return rc;
   if (int rc = grow(&c->d_ws, &c->cap_ws, ws)) return rc;
-  cudaError_t e = cudaMemcpyAsync(c->d_x, x, batch * in_dim * sizeof(float), cudaMemcpyHostToDevice, c->stream);
+  if (int rc = grow_pinned(&c->h_x, &c->cap_hx, batch * in_dim)) return rc;
+  if (int rc = grow_pinned(&c->h_ws, &c->cap_hws, ws)) return rc;
+  // one pinned copy in, the GEMV and the exchange, one pinned copy of the
+  // whole gather buffer out; the host then reorders [rank][b][rpr] -> [b][out]
+  memcpy(c->h_x, x, batch * in_dim * sizeof(float));
+  cudaError_t e = cudaMemcpyAsync(c->d_x, c->h_x, batch * in_dim * sizeof(float), cudaMemcpyHostToDevice, c->stream);
   if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard x copy: %s", cudaGetErrorString(e));
   if (int rc = m3g_shard_matvec_dev(c, tidx, c->d_x, batch, c->d_ws, c->stream)) return rc;
-  // gather layout [rank][b][rpr] -> [b][out]
+  e = cudaMemcpyAsync(c->h_ws, c->d_ws, ws * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
+  if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard y copy: %s", cudaGetErrorString(e));
+  e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard sync: %s", cudaGetErrorString(e));
   for (uint64_t b = 0; b < batch; ++b) {
     for (int r = 0; r < c->world; ++r) {
       const uint64_t r0 = std::min<uint64_t>(out_dim, t.rpr * r), r1 = std::min<uint64_t>(out_dim, t.rpr * (r + 1));
-      if (r1 <= r0) continue;
-      e = cudaMemcpyAsync(y + b * out_dim + r0, c->d_ws + (static_cast<uint64_t>(r) * batch + b) * t.rpr,
-                          (r1 - r0) * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
-      if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard y copy: %s", cudaGetErrorString(e));
+      if (r1 > r0)
+        memcpy(y + b * out_dim + r0, c->h_ws + (static_cast<uint64_t>(r) * batch + b) * t.rpr,
+               (r1 - r0) * sizeof(float));
     }
   }
-  e = cudaStreamSynchronize(c->stream);
-  if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard sync: %s", cudaGetErrorString(e));
   return M3G_OK;
 }
 
