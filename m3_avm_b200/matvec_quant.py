@@ -31,7 +31,16 @@ def matvec_quant(x, raw, dtype: int, in_dim: int, out_dim: int):
     """src/matvec_quant.rs:87-109: Some(y) as a float32 array, or None."""
     xa = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
     r = _u8(raw)
-    y = np.empty(max(out_dim, 1), np.float32)
+    # the reference's checks, in its order, before anything is allocated
+    if xa.size != in_dim or in_dim == 0 or out_dim == 0:
+        return None
+    n = in_dim * out_dim
+    if n >= 1 << 64:  # checked_mul overflows usize
+        return None
+    need = quant_raw_len(dtype, n)
+    if need is None or r.size < need:
+        return None
+    y = np.empty(out_dim, np.float32)
     rc = _lib.load().m3g_matvec_quant(xa.ctypes.data, xa.size, r.ctypes.data, r.size, dtype, in_dim, out_dim,
                                       y.ctypes.data)
     if rc == _lib.M3G_ENONE:

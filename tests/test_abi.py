@@ -96,7 +96,24 @@ def test_python_mirror_none_rules_without_device():
     assert M.matvec_quant(x8, bytes(10), 12, 32, 8) is None
     assert M.matvec_quant(x8, bytes(144), 12, 7, 5) is None
     assert M.matvec_quant(np.ones(4, np.float32), bytes(144), 12, 16, 16) is None
+    # src/matvec_quant.rs:94-97: empty shapes and an overflowing in_dim * out_dim
+    assert M.matvec_quant(np.zeros(0, np.float32), bytes(144), 12, 0, 16) is None
+    assert M.matvec_quant(np.ones(256, np.float32), bytes(144), 12, 256, 0) is None
+    assert M.matvec_quant(np.ones(256, np.float32), bytes(144), 12, 256, 2 ** 62) is None
     assert M.quant_raw_len(12, 512) == 288 and M.quant_raw_len(0, 512) is None
+
+
+def test_c_abi_none_rules_without_device(lib):
+    """The C entry point answers M3G_ENONE for empty shapes and an overflowing
+    in_dim * out_dim before any device work (src/matvec_quant.rs:94-97)."""
+    x = np.ones(256, np.float32)
+    raw = np.zeros(144, np.uint8)
+    y = np.zeros(4, np.float32)
+    for in_dim, out_dim in [(0, 16), (256, 0), (256, 2 ** 62), (2 ** 40, 2 ** 40)]:
+        rc = lib.m3g_matvec_quant(x.ctypes.data, min(in_dim, x.size), raw.ctypes.data, raw.size, 12, in_dim,
+                                  out_dim, y.ctypes.data)
+        assert rc == -1, (in_dim, out_dim, rc)
+    assert np.all(y == 0)
 
 
 @pytest.mark.skipif(HAS_CUDA, reason="checks the no-device error path")
