@@ -17,9 +17,11 @@
 //  * otherwise (the default) one in-place NCCL all-gather of the fp32 slices.
 //
 // Measured on 2 B200s (Q4_K 14336 x 4096 per call): the local rows alone take
-// 6.0 us, with the NCCL all-gather 16.4 us, with peer stores 22.0 us (the
-// system-scope fences, the arrival atomics and the separate gather launch
-// cost more than NCCL's own kernel), so NCCL is the default.
+// 6.0 us, with the NCCL all-gather 16.4-18.2 us, with peer stores 19.3 us.
+// A stamped copy shows where the peer-store form goes: each CTA's
+// system-scope fence after its remote stores takes ~3.4 us, the last CTA's
+// fence and arrival atomics ~3.7 us (a release reduction instead waited as
+// long), then the gather.  NCCL stays the default.
 //
 // Communicator creation is non-blocking with a wall-clock limit: a rank that
 // never joins makes create() abort the communicator and return M3G_ETIMEOUT
@@ -174,6 +176,9 @@ __global__ void __launch_bounds__(256) k_shard_gather(uint8_t* region, unsigned 
                                                       long long rpr_cap, float* __restrict__ y, long long n,
                                                       uint32_t* status, unsigned long long wait_ns) {
   m3g::grid_dep_wait();
+  // The next call's GEMV may start streaming its weights; it reads this
+  // region's step and writes peers' rows only after its own grid dependency.
+  m3g::grid_dep_launch();
   const unsigned* arr = reinterpret_cast<const unsigned*>(region + kArrOff);
   int* step = reinterpret_cast<int*>(region + kStepOff);
   __shared__ int s_step;
@@ -512,11 +517,22 @@ int m3g_shard_matvec_dev(m3g_shard* c, uint64_t tidx, const float* x, uint64_t b
     uint32_t* status = nullptr;
     if (int rc = m3g::status_word(c->device, &status)) return rc;
     const long long n = static_cast<long long>(c->world) * static_cast<long long>(t.rpr);
-    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(64, (n + 4095) / 4096)));
-    k_shard_gather<<<grid, 256, 0, st>>>(c->region, static_cast<unsigned>(c->world), c->rank,
-                                         static_cast<long long>(t.rpr), static_cast<long long>(c->rpr_cap), y, n,
-                                         status, m3g::peer_wait_ns());
-    cudaError_t e = cudaGetLastError();
+    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(512, (n + 255) / 256)));
+    // Programmatic dependent launch: the gather's CTAs (256 threads, no
+    // shared memory) fit beside the GEMV's and wait in griddepcontrol.wait,
+    // so no launch gap separates the two.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_shard_gather, c->region, static_cast<unsigned>(c->world), c->rank,
+                                       static_cast<long long>(t.rpr), static_cast<long long>(c->rpr_cap), y, n,
+                                       status, m3g::peer_wait_ns());
     if (e != cudaSuccess) return m3g::host_fail(M3G_ECUDA, "shard gather launch: %s", cudaGetErrorString(e));
     ++c->calls;
     return M3G_OK;
