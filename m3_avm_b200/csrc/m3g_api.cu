@@ -240,6 +240,11 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   if (sbb == 0 || RB % 16 || reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16) return false;
   if (rows > (1ll << 31) - 1 || in_dim > (1 << 20)) return false;
   long long KC = std::min<long long>(NSB, std::min<int64_t>(16, g_tune.mma_kc));
+  // Q8_0 rows take 4352 bytes per 4096 inputs, so a 16-row stage of 16
+  // super-blocks is 70 KB and only two or three fit: half-width k-chunks keep
+  // the ring deep (measured 4096x4096: 8.0 -> 6.45 us; 14336x4096: 18.1 ->
+  // 17.6 us).  Q4_K, Q4_0 and Q6_K are slower with them.
+  if (f.fmt == 8 && g_tune.mma_kc == 16 && NSB >= 16) KC = 8;
   // Consumer warps per tile: 16 when a k-chunk of 16 super-blocks covers the
   // whole row (one super-block per warp, x operands stay in registers), or
   // for the heavier Q6_K decode; 8 otherwise.  mma_wk = 8 / 16 forces it.
