@@ -158,10 +158,11 @@ M3G_API void m3g_offload_destroy(m3g_offload* ctx);
 /* One process per GPU.  Rank r keeps output rows [r*RPR, min(out, (r+1)*RPR))
  * of each tensor, RPR = ceil(out_dim / world); a matvec computes the local
  * rows and every rank receives the whole fp32 output: by one in-place NCCL
- * all-gather of the fp32 slices, or -- tuning key "shard_p2p" set to 1 before
- * creation, batch 1, a tensor-core plan for the shape, and every rank able to
- * map every other rank's region -- by peer stores from the GEMV's epilogue
- * into every rank's exchange region over NVLink.  No counterpart in the
+ * all-gather of the fp32 slices, or -- when the tuning key "shard_p2p" at
+ * creation selects it (1; the default -1 selects it from 8 ranks up, where it
+ * measured faster, 0 never), batch 1, a tensor-core plan for the shape, and
+ * every rank able to map every other rank's region -- by peer stores from the
+ * GEMV's epilogue into every rank's exchange region over NVLink.  No counterpart in the
  * reference (it is single-host, single-CPU); this is the sharded form of the
  * GpuOffload shape above. */
 typedef struct m3g_shard m3g_shard;

@@ -101,7 +101,8 @@ struct Tuning {
   int64_t peer_wait_us = 2000000; // limit of a kernel's wait for a counter bumped by other GPUs
   int64_t mma_tail_first = 1;     // tensor-core GEMV: a CTA's partial row group first
   int64_t offload_mapped = 1;     // batch-1 host-buffer calls: x, y, status through mapped pinned memory
-  int64_t shard_p2p = 0;          // shard contexts: rows exchanged by peer stores from the GEMV epilogue (else NCCL)
+  int64_t shard_p2p = -1;         // shard contexts: 1 rows exchanged by peer stores from the GEMV epilogue, 0 NCCL,
+                                  // -1 peer stores from 8 ranks up (measured faster there, NCCL below)
   int64_t tc8 = 0;                // batch-1 Q4_K GEMV on tcgen05 kind::i8 (k_tc8_q4k, K <= 4096)
   int64_t tc8_pre = 0;            // k_tc8_q4k stages streamed before x is loaded (0: all)
 };
@@ -685,7 +686,7 @@ int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const flo
 }
 
 bool decode_p2p_enabled() { return g_tune.decode_p2p != 0; }
-bool shard_p2p_enabled() { return g_tune.shard_p2p != 0; }
+bool shard_p2p_enabled(int world) { return g_tune.shard_p2p > 0 || (g_tune.shard_p2p < 0 && world >= 8); }
 
 bool fused_plannable(int device, uint32_t dtype, long long in_dim, long long rows) {
   FmtInfo f;
@@ -756,7 +757,7 @@ int m3g_set_tuning(const char* key, int64_t value) {
   else if (!strcmp(key, "peer_wait_us") && value >= 1 && value <= 60000000) g_tune.peer_wait_us = value;
   else if (!strcmp(key, "mma_tail_first")) g_tune.mma_tail_first = value != 0;
   else if (!strcmp(key, "offload_mapped")) g_tune.offload_mapped = value != 0;
-  else if (!strcmp(key, "shard_p2p")) g_tune.shard_p2p = value != 0;
+  else if (!strcmp(key, "shard_p2p") && value >= -1 && value <= 1) g_tune.shard_p2p = value;
   else if (!strcmp(key, "tc8")) g_tune.tc8 = value != 0;
   else if (!strcmp(key, "tc8_pre") && value >= 0 && value <= 64) g_tune.tc8_pre = value;
   else return fail(M3G_ENONE, "unknown tuning key or value: %s=%lld", key, static_cast<long long>(value));

@@ -155,7 +155,7 @@ int gemv_greedy_on(uint32_t dtype, const uint8_t* w, uint64_t raw_len, const flo
 unsigned long long peer_wait_ns();
 
 // Whether a shard context may exchange rows by peer stores (tuning knob).
-bool shard_p2p_enabled();
+bool shard_p2p_enabled(int world);
 // Whether the tensor-core GEMV has a plan for `rows` rows of `in_dim` inputs
 // of `dtype` on `device` (16-byte aligned weights and input assumed).
 bool fused_plannable(int device, uint32_t dtype, long long in_dim, long long rows);

@@ -386,7 +386,7 @@ int m3g_shard_create(int device, int rank, int world, const uint8_t* id128, uint
   // Peer-store exchange region.  Every rank makes the same decision (the
   // tuning key is process-wide) and joins the collective agreement, even one
   // whose allocation failed: it then votes no and every rank keeps NCCL.
-  if (world > 1 && world <= m3g::kMaxPeers && m3g::shard_p2p_enabled()) {
+  if (world > 1 && world <= m3g::kMaxPeers && m3g::shard_p2p_enabled(world)) {
     c->rpr_cap = (max_out + world - 1) / world;
     const size_t bytes = kRowsOff + 2 * static_cast<size_t>(world) * c->rpr_cap * sizeof(float);
     cudaError_t ea = cudaMalloc(&c->region, bytes);

@@ -2,9 +2,11 @@
 
 Rank r of `world` keeps output rows [r*RPR, min(out, (r+1)*RPR)) of each
 tensor, RPR = ceil(out_dim / world); ``matvec`` computes the local rows and
-every rank receives the full fp32 output: by peer stores from the GEMV
-epilogue over NVLink where the ranks can map each other's exchange regions
-(``exchange == "peer-stores"``), else by one NCCL all-gather.  This is the
+every rank receives the full fp32 output: by one NCCL all-gather, or by peer
+stores from the GEMV epilogue over NVLink (``exchange == "peer-stores"``)
+where the ranks can map each other's exchange regions and the tuning key
+``shard_p2p`` at creation asks for them (1; the default -1 from 8 ranks up,
+where they measured faster).  This is the
 multi-GPU form of the resident-weight offload (``inference_gpu.GpuOffload``);
 the reference runs on one host CPU and has no counterpart.
 """
