@@ -438,6 +438,10 @@ struct m3g_decoder {
   bool pending = false;  // tokens[pos] holds the greedy pick of the last step
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  // Prompt steps before the last need no logits: one GPU replays this graph,
+  // the step without the vocab head, for them.
+  cudaGraph_t graph_nohead = nullptr;
+  cudaGraphExec_t exec_nohead = nullptr;
   bool use_graph = true;
   uint64_t steps = 0;
 };
@@ -581,7 +585,9 @@ int gemv(m3g_decoder* d, const Gemv& g, const float* x, const float* x2, const f
 }
 
 // Enqueue one decode step on d->st (also the body the graph captures).
-int enqueue_step(m3g_decoder* d) {
+// head = false (one GPU only) leaves out the vocab head GEMV: the pick then
+// reads the cleared key and, the next token being a prompt token, writes none.
+int enqueue_step(m3g_decoder* d, bool head = true) {
   const int h = static_cast<int>(d->cfg.hidden), F = static_cast<int>(d->cfg.ffn);
   const int L = static_cast<int>(d->cfg.n_layers), V = static_cast<int>(d->cfg.vocab);
   const int mp = static_cast<int>(d->cfg.max_pos);
@@ -708,7 +714,7 @@ int enqueue_step(m3g_decoder* d) {
     if (pp_ffn) wait_on(hio, 2 * (L - 1) + 1);
     ph = &hio;
   }
-  if (H.out > 0) {  // the last rank of a small vocabulary may hold no rows (NCCL path only)
+  if (H.out > 0 && (head || d->world > 1)) {  // the last rank of a small vocabulary may hold no rows (NCCL path only)
     if (int rc = m3g::gemv_fused(d->device, H.dtype, H.d, H.len, d->hidden, nullptr, g_out, nullptr, m3g::kXRmsNorm,
                                  d->logits + H.row0, H.in, H.out, d->st, true, d->key, false, H.row0, ph))
       return rc;
@@ -728,21 +734,30 @@ int enqueue_step(m3g_decoder* d) {
 void drop_graph(m3g_decoder* d) {
   if (d->exec) cudaGraphExecDestroy(d->exec);
   if (d->graph) cudaGraphDestroy(d->graph);
+  if (d->exec_nohead) cudaGraphExecDestroy(d->exec_nohead);
+  if (d->graph_nohead) cudaGraphDestroy(d->graph_nohead);
   d->exec = nullptr;
   d->graph = nullptr;
+  d->exec_nohead = nullptr;
+  d->graph_nohead = nullptr;
 }
 
 // Run `n` steps.  The first step of a decoder runs eagerly (it also sets up
 // every kernel's shared-memory limit); later ones replay the captured graph.
-int run_steps(m3g_decoder* d, uint64_t n) {
+// prompt: the steps feed prompt tokens, and only the last one's logits are
+// wanted.
+int run_steps(m3g_decoder* d, uint64_t n, bool prompt = false) {
   if (int rc = prepare(d)) return rc;
   if (d->pos + n > d->cfg.max_pos)
     return host_fail(M3G_EINVAL, "%llu steps from position %d overflow the KV cache of %llu positions",
                      static_cast<unsigned long long>(n), d->pos, static_cast<unsigned long long>(d->cfg.max_pos));
   for (uint64_t i = 0; i < n; ++i) {
-    if (d->use_graph && d->steps > 0 && !d->exec) {
+    const bool head = !(prompt && d->world == 1 && d->steps > 0 && i + 1 < n);
+    cudaGraph_t& graph = head ? d->graph : d->graph_nohead;
+    cudaGraphExec_t& exec = head ? d->exec : d->exec_nohead;
+    if (d->use_graph && d->steps > 0 && !exec) {
       DEC_CUDA(cudaStreamBeginCapture(d->st, cudaStreamCaptureModeThreadLocal));
-      const int rc = enqueue_step(d);
+      const int rc = enqueue_step(d, head);
       cudaGraph_t g = nullptr;
       const cudaError_t e = cudaStreamEndCapture(d->st, &g);
       if (rc) {
@@ -750,12 +765,12 @@ int run_steps(m3g_decoder* d, uint64_t n) {
         return rc;
       }
       if (e != cudaSuccess) return host_fail(M3G_ECUDA, "decode step capture: %s", cudaGetErrorString(e));
-      d->graph = g;
-      DEC_CUDA(cudaGraphInstantiate(&d->exec, d->graph, 0));
+      graph = g;
+      DEC_CUDA(cudaGraphInstantiate(&exec, graph, 0));
     }
-    if (d->exec) {
-      DEC_CUDA(cudaGraphLaunch(d->exec, d->st));
-    } else if (int rc = enqueue_step(d)) {
+    if (exec) {
+      DEC_CUDA(cudaGraphLaunch(exec, d->st));
+    } else if (int rc = enqueue_step(d, head)) {
       return rc;
     }
     ++d->steps;
@@ -1066,7 +1081,7 @@ M3G_API int m3g_decoder_prefill(m3g_decoder* d, const uint32_t* tokens, uint64_t
   DEC_CUDA(cudaMemcpy(d->tokens + d->pos, tokens, 4 * n, cudaMemcpyHostToDevice));
   const int nfixed = d->pos + static_cast<int>(n);
   DEC_CUDA(cudaMemcpy(d->nfixed, &nfixed, 4, cudaMemcpyHostToDevice));
-  if (int rc = run_steps(d, n)) return rc;
+  if (int rc = run_steps(d, n, true)) return rc;
   if (int rc = gather_logits(d, logits != nullptr)) return rc;
   if (logits) DEC_CUDA(cudaMemcpyAsync(logits, d->logits, 4 * d->cfg.vocab, cudaMemcpyDeviceToHost, d->st));
   return check_status(d);
