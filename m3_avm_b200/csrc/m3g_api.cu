@@ -249,14 +249,19 @@ bool plan_mma(const FmtInfo& f, long long in_dim, long long rows, const uint8_t*
   // Consumer warps per tile: 16 when a k-chunk of 16 super-blocks covers the
   // whole row (one super-block per warp, x operands stay in registers), or
   // for the heavier Q6_K decode; 8 otherwise.  mma_wk = 8 / 16 forces it.
+  const long long rows_per_sm = (rows + ds.sms - 1) / ds.sms;
+  // Q6_K rows of 16 super-blocks with very many rows per SM (the 128256-row
+  // vocab head: 867) run 3 % faster as two 8-warp tiles per stage; at 221
+  // rows per SM (32768 rows) and below that form is slower.
+  const bool q6k_many = f.fmt == 14 && NSB == 16 && KC == 16 && rows_per_sm >= 512;
   int wk = g_tune.mma_wk;
-  if (wk != 8 && wk != 16) wk = ((NSB == 16 && KC == 16) || (f.fmt == 14 && NSB >= 16)) ? 16 : 8;
+  if (wk != 8 && wk != 16)
+    wk = q6k_many ? 8 : (((NSB == 16 && KC == 16) || (f.fmt == 14 && NSB >= 16)) ? 16 : 8);
   // Two 8-warp tiles per stage (16 consumer warps) pay off when each CTA
   // streams many short rows (measured: Q6_K 128256x2048 -31 %, Q4_K
   // 16384x2048 -10 %) and cost on small or long-row shapes (2048x2048 +19 %,
   // 28672x8192 +3 %).
-  const long long rows_per_sm = (rows + ds.sms - 1) / ds.sms;
-  const int auto_tps = NSB <= 8 && rows_per_sm >= 64 ? 2 : 1;
+  const int auto_tps = (NSB <= 8 && rows_per_sm >= 64) || q6k_many ? 2 : 1;
   const int tps = wk == 16 ? 1 : (g_tune.mma_tps == 0 ? auto_tps : static_cast<int>(std::min<int64_t>(2, g_tune.mma_tps)));
   if (f.fmt == 14) {  // 210-byte blocks: chunk sizes must stay multiples of 16 bytes
     if (NSB % 8) return false;

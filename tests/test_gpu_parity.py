@@ -152,7 +152,7 @@ KERNELS = {
     "stream": {"mma": 0},
     "generic": {"force_generic": 1},
 }
-DEFAULT_TUNING = {"mma": 1, "force_generic": 0, "mma_tps": 1, "mma_kc": 16, "mma_ctas": 1, "mma_wk": 0, "mma_cg": 4, "mma_coresident": 0, "mma_pre": 1}
+DEFAULT_TUNING = {"mma": 1, "force_generic": 0, "mma_tps": 0, "mma_kc": 16, "mma_ctas": 1, "mma_wk": 0, "mma_cg": 4, "mma_coresident": 0, "mma_pre": 1}
 
 
 @pytest.fixture(params=list(KERNELS))
